@@ -1,0 +1,186 @@
+/* picchio_b200.h - C ABI of the B200 (sm_100a) implementation of picchio's
+ * per-token MoE hot path.
+ *
+ * The reference (benmaster82/picchio) keeps its engine in one C translation
+ * unit with static functions; the entry points below are the ones a C host
+ * (picchio.c's main / service_loop, or any FFI) binds in place of them.  Each
+ * declaration names the reference interface it replaces.
+ *
+ * Conventions
+ *  - Every call returns a pc_status; nothing calls exit().  pc_last_error()
+ *    gives a one-line description of the last failure on the calling thread.
+ *  - One pc_ctx per GPU (per expert-parallel rank).  Calls on a context are
+ *    ordered on the context's CUDA stream and return after the results they
+ *    promise are on the host.  A context is not thread-safe (nor is the
+ *    reference: it keeps its state in globals).
+ *  - Pointers named *_dev are device pointers; all others are host memory.
+ *  - No torch types, no C++ types: plain pointers and sizes.
+ */
+#ifndef PICCHIO_B200_H
+#define PICCHIO_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum {
+    PC_OK = 0,
+    PC_ERR_INVALID_ARG = 1,    /* null pointer, bad size, bad option */
+    PC_ERR_IO = 2,             /* model directory or file unreadable */
+    PC_ERR_FORMAT = 3,         /* tensor dtype / shape / group size not supported */
+    PC_ERR_MISSING_TENSOR = 4, /* a required tensor is absent (e.g. sinks, an expert) */
+    PC_ERR_CUDA = 5,           /* a CUDA runtime call failed */
+    PC_ERR_OOM = 6,            /* device or pinned-host allocation failed */
+    PC_ERR_RANGE = 7,          /* token id, position or batch outside the context */
+    PC_ERR_TIMEOUT = 8,        /* a bounded device-side wait gave up */
+    PC_ERR_NCCL = 9,           /* NCCL unavailable or a collective failed */
+    PC_ERR_STATE = 10          /* call not valid in the context's current state */
+} pc_status;
+
+typedef struct pc_ctx pc_ctx;
+typedef struct pc_qt pc_qt;
+
+/* Weight formats, as quant.h:32-41 numbers them (QT.fmt). */
+enum { PC_FMT_F32 = 0, PC_FMT_INT8 = 1, PC_FMT_INT4 = 2 };
+
+typedef struct {
+    int device;        /* CUDA device ordinal */
+    int ctx_len;       /* KV positions per sequence (env CTX; reference default 512) */
+    int kv_bf16;       /* 1: bf16 KV cache; 0: fp32, the reference's precision */
+    int max_batch;     /* sequences served by pc_decode_batch (>= 1) */
+    int ep_rank;       /* expert-parallel rank (0 when ep_size <= 1) */
+    int ep_size;       /* expert-parallel group size; <= 1 means one GPU */
+    const void *nccl_id; /* 128-byte ncclUniqueId from rank 0 when ep_size > 1 */
+    int use_graphs;    /* 1: replay decode steps as CUDA graphs */
+    int expert_residency; /* 0: whole expert table in HBM; 1: pinned host + HBM cache */
+    int expert_cache_slots; /* per layer, when expert_residency == 1 */
+} pc_opts;
+
+/* Model shape (the fields cfg_load reads, picchio.c:349-425). */
+typedef struct {
+    int hidden;          /* D */
+    int n_layers;
+    int n_heads;
+    int n_kv_heads;
+    int head_dim;
+    int n_experts;
+    int topk;
+    int intermediate;    /* intermediate_size; gate_up has 2x rows */
+    int vocab;
+    int ctx_len;         /* max_position_embeddings */
+    int sliding_window;
+    float eps;
+    float theta;
+    float swiglu_limit;
+    float swiglu_alpha;
+    float routed_scale;
+    float rope_factor, rope_beta_fast, rope_beta_slow;
+    int rope_original_ctx, rope_truncate;
+    int group_size;      /* expert INT4 group size (0 = per-row scale) */
+    int attn_format;     /* PC_FMT_* of q/k/v/o */
+    int attn_group_size; /* group size when attn_format == PC_FMT_INT4 */
+    int layer_type[256]; /* 0 sliding, 1 full (picchio.c:389-409) */
+} pc_model_cfg;
+
+/* Fills *o with the defaults (device 0, ctx 512, fp32 KV, batch 1, graphs on). */
+void pc_default_opts(pc_opts *o);
+
+/* Status name and the calling thread's last error message. */
+const char *pc_status_string(pc_status s);
+const char *pc_last_error(void);
+
+/* Loads config.json and the safetensors shards of `model_dir` the way
+ * picchio's main does (picchio.c:2836-3000: cfg_load, shard discovery,
+ * load_dense_weights picchio.c:2531-2650) and uploads every dense weight and
+ * the whole expert table (replacing the disk-streamed LRU of
+ * picchio.c:1000-1068, expert_load picchio.c:698-888) to HBM. */
+pc_status pc_init(const char *model_dir, const pc_opts *opts, pc_ctx **out);
+
+/* Same model family with seeded random weights generated on the device:
+ * N(0, 0.02) quantized as the reference converter does (convert.py:45-126).
+ * Used for shapes too large to write as files (GPT-OSS-20B/120B). */
+pc_status pc_init_synthetic(const pc_model_cfg *cfg, uint64_t seed, const pc_opts *opts,
+                            pc_ctx **out);
+
+void pc_free(pc_ctx *ctx);
+
+/* The configuration in use (after config.json parsing). */
+pc_status pc_get_config(const pc_ctx *ctx, pc_model_cfg *cfg);
+
+/* One decode step: replaces forward_token (picchio.c:1655-1756) with greedy
+ * sampling (sample_logits at TEMPERATURE=0, picchio.c:1555-1560).  Writes the
+ * next id to *next_tok.  tok outside [0, vocab) embeds as zeros like
+ * embed_token (picchio.c:1478-1481). */
+pc_status pc_forward_token(pc_ctx *ctx, int tok, int pos, int *next_tok);
+
+/* Prompt encoding: replaces prefill_tokens (picchio.c:1936-1975).  Returns
+ * the greedy id after the last position. */
+pc_status pc_prefill(pc_ctx *ctx, const int *ids, int n, int pos_base, int *next_tok);
+
+/* B independent sequences, one token each (sequence b uses KV slot b): the
+ * batched-decode form of forward_token.  B <= opts.max_batch. */
+pc_status pc_decode_batch(pc_ctx *ctx, const int *toks, const int *pos, int B, int *next);
+
+/* Copies the logits of the last step (row `row` of a batch) to the host. */
+pc_status pc_get_logits(pc_ctx *ctx, int row, float *logits, int n);
+
+/* The MoE block of one layer on M rows: replaces moe_forward
+ * (picchio.c:1309-1466): router + top-k + softmax, gate_up + bias + clamped
+ * SwiGLU, down + bias, weighted combine.  x_dev [M][D] are the normalized
+ * hidden states, out_dev [M][D] receives the MoE output (no residual). */
+pc_status pc_moe_layer(pc_ctx *ctx, int layer, const float *x_dev, float *out_dev, int M);
+
+/* The expert part of moe_forward with the routing given (sel_dev [M][K]
+ * expert ids, w_dev [M][K] combine weights): expert_apply
+ * (picchio.c:1769-1791) for every (row, k) and the combine in k order. */
+pc_status pc_moe_experts(pc_ctx *ctx, int layer, const float *x_dev, const int *sel_dev,
+                         const float *w_dev, int M, float *out_dev);
+
+/* Stage tensors of the last pc_forward_token, under the names the reference's
+ * ORACLE_DIR dump uses (picchio.c:204-249), e.g. "layer0.pre_moe_norm".
+ * Requires pc_set_trace(ctx, 1) before the step. */
+pc_status pc_set_trace(pc_ctx *ctx, int on);
+pc_status pc_get_stage(pc_ctx *ctx, const char *name, float *out, int n);
+pc_status pc_dump(pc_ctx *ctx, const char *dir);  /* writes <name>.npy like ORACLE_DIR */
+
+/* Expert residency with streaming (opts.expert_residency == 1): copies the
+ * listed experts of `layer` from pinned host memory into the layer's HBM cache
+ * on the side stream, like prefetch_issue (picchio.c:1180-1230) but exact. */
+pc_status pc_expert_prefetch(pc_ctx *ctx, int layer, const int *eids, int n);
+
+/* ---- weight-level operator: matmul_qt (quant.h:323-337) ---------------- */
+
+/* Uploads one QT weight in the reference's host layout (quant.h:32-41):
+ * fmt PC_FMT_F32: data = float[O*I]; PC_FMT_INT8: data = int8[O*I], scales =
+ * float[O]; PC_FMT_INT4: data = packed nibbles [O][ceil(I/2)] (low nibble =
+ * even column, value = nibble - 8), scales = float[O] (block_size 0) or
+ * float[O][ceil(I/gs)] (block_size = gs). */
+pc_status pc_qt_create(int device, int fmt, int O, int I, int block_size, const void *data,
+                       const float *scales, pc_qt **out);
+/* y_dev[S][O] = x_dev[S][I] . W^T on `stream` (a cudaStream_t, NULL = default). */
+pc_status pc_qt_matmul(pc_qt *w, const float *x_dev, float *y_dev, int S, void *stream);
+/* out_dev[O][I] = dequantized weights, (nibble-8)*scale in fp32. */
+pc_status pc_qt_dequant(pc_qt *w, float *out_dev, void *stream);
+void pc_qt_free(pc_qt *w);
+
+/* ---- expert parallelism -------------------------------------------------- */
+
+/* Writes a fresh 128-byte ncclUniqueId (rank 0 calls this and shares it). */
+pc_status pc_nccl_unique_id(void *out128);
+
+/* ---- diagnostics ---------------------------------------------------------- */
+
+/* Returns PC_ERR_TIMEOUT if a device-side bounded wait has given up since the
+ * last call (and clears the flag), else PC_OK. */
+pc_status pc_check_device(pc_ctx *ctx);
+
+/* Counts kernels this library launched on the context (for measurement). */
+uint64_t pc_kernel_launches(const pc_ctx *ctx);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* PICCHIO_B200_H */

@@ -1,0 +1,766 @@
+// model.cu - the forward step on the device and the C ABI (picchio_b200.h).
+//
+// One step processes M token rows (a decode batch, or a prefill chunk of one
+// sequence), in the layer order of forward_token (picchio.c:1655-1756):
+//   embed -> per layer { rmsnorm, q/k/v GEMV + bias + RoPE + KV store,
+//   attention, o GEMV + bias + residual, rmsnorm, router + top-k + softmax,
+//   gate_up GEMV + bias + SwiGLU, down GEMV + bias, weighted combine +
+//   residual } -> rmsnorm -> lm_head GEMV + greedy argmax.
+// Decode steps are captured once per shape in a CUDA graph and replayed.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "context.h"
+#include "ep.h"
+#include "gemv.h"
+#include "host_io.h"
+#include "kernels.h"
+
+namespace pc {
+
+thread_local std::string g_last_error;
+
+pc_status fail(pc_status s, const std::string &msg) {
+    g_last_error = msg;
+    return s;
+}
+
+pc_status cuda_fail(cudaError_t e, const char *what) {
+    return fail(e == cudaErrorMemoryAllocation ? PC_ERR_OOM : PC_ERR_CUDA,
+                std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+namespace {
+std::mutex g_cfg_mu;
+bool g_configured[64] = {false};
+}  // namespace
+
+pc_status device_setup(int dev, int *nsm, int *max_smem) {
+    PC_CU(cudaSetDevice(dev));
+    cudaDeviceProp prop;
+    PC_CU(cudaGetDeviceProperties(&prop, dev));
+    if (prop.major < 10) return fail(PC_ERR_CUDA, std::string("device ") + prop.name + " is not sm_100 (B200)");
+    *nsm = prop.multiProcessorCount;
+    *max_smem = (int)prop.sharedMemPerBlockOptin;
+    std::lock_guard<std::mutex> lk(g_cfg_mu);
+    if (dev >= 0 && dev < 64 && !g_configured[dev]) {
+        PC_CU(gemv_configure(*max_smem));
+        g_configured[dev] = true;
+    }
+    return PC_OK;
+}
+
+pc_status dalloc(pc_ctx *c, size_t bytes, void **out) {
+    *out = nullptr;
+    if (bytes == 0) bytes = 16;
+    cudaError_t e = cudaMalloc(out, bytes);
+    if (e != cudaSuccess) return fail(PC_ERR_OOM, "cudaMalloc(" + std::to_string(bytes) + "): " + cudaGetErrorString(e));
+    e = cudaMemset(*out, 0, bytes);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMemset");
+    c->allocs.push_back(*out);
+    return PC_OK;
+}
+
+namespace {
+
+pc_status configure_device(pc_ctx *c) { return device_setup(c->dev, &c->nsm, &c->max_smem); }
+
+int nt_for_rows(int rows) { return rows <= 4 ? 1 : 2; }
+
+// CUDA events around one launch while profiling (pc_profile_begin/end).
+struct Prof {
+    pc_ctx *c;
+    const char *label;
+    cudaEvent_t a = nullptr, b = nullptr;
+    Prof(pc_ctx *cc, const char *l) : c(cc), label(l) {
+        if (!c->prof) return;
+        cudaEventCreate(&a);
+        cudaEventCreate(&b);
+        cudaEventRecord(a, c->st);
+    }
+    ~Prof() {
+        if (!a) return;
+        cudaEventRecord(b, c->st);
+        c->prof_evs.push_back({label, a, b});
+    }
+};
+
+// Launch one GEMV over a device job list.
+pc_status run_gemv(pc_ctx *c, GemvParams p, int rows_per_job, const char *label) {
+    p.err = c->err;
+    const int nt = nt_for_rows(rows_per_job);
+    if (!gemv_plan(p, nt, c->max_smem))
+        return fail(PC_ERR_FORMAT, "GEMV input of " + std::to_string(p.Ip) + " columns does not fit in shared memory");
+    Prof pr(c, label);
+    PC_CU(gemv_launch(p, nt, c->nsm, c->st));
+    ++c->launches;
+    return PC_OK;
+}
+
+void params_for(GemvParams &p, const TileDesc &t, int epi) {
+    p.fmt = t.fmt;
+    p.gs = t.gs;
+    p.kblocks = t.kblocks;
+    p.blk_bytes = t.blk_bytes;
+    p.I = t.I;
+    p.Ip = t.Ip;
+    p.perm = t.perm;
+    p.head_dim = t.head_dim;
+    p.epi = epi;
+}
+
+GemvJob make_job(const TileDesc &t, const float *bias, int seg, const int *in, const int *out, int n) {
+    GemvJob j;
+    memset(&j, 0, sizeof j);
+    j.tiles = t.tiles;
+    j.rs = t.rs;
+    j.bias = bias;
+    j.n_rt = t.Op / 16;
+    j.O = t.O;
+    j.nrows = n;
+    j.seg = seg;
+    for (int i = 0; i < n; ++i) { j.in_row[i] = in[i]; j.out_row[i] = out[i]; }
+    return j;
+}
+
+// Job tables of the dense projections for M rows; lm_mode 0: logits for
+// every row, 1: last row only, 2: none.
+pc_status dense_jobs(pc_ctx *c, int M, int lm_mode, DenseJobs **out) {
+    const uint64_t key = (uint64_t)M * 4 + lm_mode;
+    auto it = c->dense_jobs.find(key);
+    if (it != c->dense_jobs.end()) { *out = &it->second; return PC_OK; }
+    DenseJobs dj;
+    std::vector<GemvJob> jobs;
+    std::vector<int> counts;
+    const int ng = (M + GEMV_MAXR - 1) / GEMV_MAXR;
+    std::vector<int> rows(M);
+    for (int i = 0; i < M; ++i) rows[i] = i;
+    for (auto &ly : c->L) {
+        dj.qkv_off.push_back((int)jobs.size());
+        dj.qkv_cnt_idx.push_back((int)counts.size());
+        int n = 0;
+        if (ly.wq.t.fmt != TF_F32) {
+            for (int g = 0; g < ng; ++g) {
+                const int r0 = g * GEMV_MAXR, nr = std::min(GEMV_MAXR, M - r0);
+                jobs.push_back(make_job(ly.wq.t, ly.wq.bias, 0, &rows[r0], &rows[r0], nr));
+                jobs.push_back(make_job(ly.wk.t, ly.wk.bias, 1, &rows[r0], &rows[r0], nr));
+                jobs.push_back(make_job(ly.wv.t, ly.wv.bias, 2, &rows[r0], &rows[r0], nr));
+                n += 3;
+            }
+        }
+        counts.push_back(n);
+        dj.o_off.push_back((int)jobs.size());
+        dj.o_cnt_idx.push_back((int)counts.size());
+        n = 0;
+        if (ly.wo.t.fmt != TF_F32) {
+            for (int g = 0; g < ng; ++g) {
+                const int r0 = g * GEMV_MAXR, nr = std::min(GEMV_MAXR, M - r0);
+                jobs.push_back(make_job(ly.wo.t, ly.wo.bias, 0, &rows[r0], &rows[r0], nr));
+                ++n;
+            }
+        }
+        counts.push_back(n);
+    }
+    dj.lm_off = (int)jobs.size();
+    dj.lm_cnt_idx = (int)counts.size();
+    int n = 0;
+    if (lm_mode != 2 && c->lm_head.t.fmt != TF_F32) {
+        if (lm_mode == 1) {
+            const int in = M - 1, o = 0;
+            jobs.push_back(make_job(c->lm_head.t, nullptr, 0, &in, &o, 1));
+            n = 1;
+        } else {
+            for (int g = 0; g < ng; ++g) {
+                const int r0 = g * GEMV_MAXR, nr = std::min(GEMV_MAXR, M - r0);
+                jobs.push_back(make_job(c->lm_head.t, nullptr, 0, &rows[r0], &rows[r0], nr));
+                ++n;
+            }
+        }
+    }
+    counts.push_back(n);
+    if (jobs.empty()) jobs.push_back(GemvJob{});
+    PC_TRY(dalloc(c, jobs.size() * sizeof(GemvJob), (void **)&dj.d_jobs));
+    PC_TRY(dalloc(c, counts.size() * 4, (void **)&dj.d_counts));
+    PC_CU(cudaMemcpy(dj.d_jobs, jobs.data(), jobs.size() * sizeof(GemvJob), cudaMemcpyHostToDevice));
+    PC_CU(cudaMemcpy(dj.d_counts, counts.data(), counts.size() * 4, cudaMemcpyHostToDevice));
+    auto res = c->dense_jobs.emplace(key, dj);
+    *out = &res.first->second;
+    return PC_OK;
+}
+
+void trace_row(pc_ctx *c, const std::string &name, const float *dev, int n) {
+    if (!c->trace) return;
+    std::vector<float> v(n);
+    cudaStreamSynchronize(c->st);
+    cudaMemcpy(v.data(), dev, (size_t)n * 4, cudaMemcpyDeviceToHost);
+    c->stages[name] = std::move(v);
+}
+
+void trace_row_i(pc_ctx *c, const std::string &name, const int *dev, int n) {
+    if (!c->trace) return;
+    std::vector<int> v(n);
+    cudaStreamSynchronize(c->st);
+    cudaMemcpy(v.data(), dev, (size_t)n * 4, cudaMemcpyDeviceToHost);
+    std::vector<float> f(v.begin(), v.end());
+    c->stages[name] = std::move(f);
+}
+
+// The MoE block of one layer for M rows whose normalized states are x:
+// router (or given routing), gate_up + SwiGLU, down, combine.
+pc_status run_moe(pc_ctx *c, int l, const float *x, int M, const int *sel_in, const float *w_in,
+                  int bias_first, float *out, float *h) {
+    const pc_model_cfg &k = c->cfg;
+    const int K = k.topk, D = k.hidden;
+    Layer &ly = c->L[l];
+    RouterParams r{};
+    r.x = x;
+    r.R = ly.router;
+    r.bias = ly.router_bias;
+    r.M = M;
+    r.D = D;
+    r.E = k.n_experts;
+    r.K = K;
+    r.bias_first = bias_first;
+    r.logits = c->rlogits;
+    r.sel = c->sel;
+    r.w = c->rw;
+    r.counter = c->router_ctr;
+    r.sel_in = sel_in;
+    r.w_in = w_in;
+    r.table = ly.experts;
+    r.stride = c->eg.stride;
+    r.off_gu = c->eg.off_gu;
+    r.off_dn = c->eg.off_dn;
+    r.off_gu_rs = c->eg.off_gu_rs;
+    r.off_dn_rs = c->eg.off_dn_rs;
+    r.off_gu_b = c->eg.off_gu_b;
+    r.off_dn_b = c->eg.off_dn_b;
+    r.gu_rt = c->eg.gu.Op / 16;
+    r.dn_rt = c->eg.dn.Op / 16;
+    r.gu_O = c->eg.gu.O;
+    r.dn_O = c->eg.dn.O;
+    r.e_lo = c->e_lo;
+    r.e_hi = c->e_hi;
+    r.slot_of = nullptr;
+    r.jobs_gu = c->jobs_gu;
+    r.jobs_dn = c->jobs_dn;
+    r.njobs = c->njobs;
+    r.pair_local = c->pair_local;
+    {
+        Prof pr(c, "router");
+        PC_CU(launch_router(r, c->st));
+    }
+    ++c->launches;
+    if (c->trace) {
+        const int last = M - 1;
+        trace_row(c, "layer" + std::to_string(l) + ".router_logits", c->rlogits + (size_t)last * k.n_experts, k.n_experts);
+        trace_row_i(c, "layer" + std::to_string(l) + ".top_indices", c->sel + (size_t)last * K, K);
+        trace_row(c, "layer" + std::to_string(l) + ".top_weights", c->rw + (size_t)last * K, K);
+    }
+    const int rows = std::min(M, GEMV_MAXR);
+    GemvParams p{};
+    params_for(p, c->eg.gu, EPI_SWIGLU);
+    p.jobs = c->jobs_gu;
+    p.njobs = c->njobs;
+    p.x = x;
+    p.ldx = D;
+    p.y = c->act;
+    p.ldy = k.intermediate;
+    p.swiglu_limit = k.swiglu_limit;
+    p.swiglu_alpha = k.swiglu_alpha;
+    PC_TRY(run_gemv(c, p, rows, "expert_gate_up"));
+    const bool ep = c->nccl_comm != nullptr;
+    if (ep) PC_CU(cudaMemsetAsync(c->eo, 0, (size_t)M * K * D * 4, c->st));
+    params_for(p, c->eg.dn, EPI_STORE);
+    p.jobs = c->jobs_dn;
+    p.njobs = c->njobs + 1;
+    p.x = c->act;
+    p.ldx = k.intermediate;
+    p.y = c->eo;
+    p.ldy = D;
+    PC_TRY(run_gemv(c, p, rows, "expert_down"));
+    if (ep) PC_TRY(ep_allreduce_sum(c, c->eo, (size_t)M * K * D));
+    if (c->trace) {
+        const int last = M - 1;
+        for (int kk = 0; kk < K; ++kk) {
+            trace_row(c, "layer" + std::to_string(l) + ".expert" + std::to_string(kk) + ".activated",
+                      c->act + ((size_t)last * K + kk) * k.intermediate, k.intermediate);
+            trace_row(c, "layer" + std::to_string(l) + ".expert" + std::to_string(kk) + ".output",
+                      c->eo + ((size_t)last * K + kk) * D, D);
+        }
+    }
+    PC_CU(launch_combine(c->eo, c->rw, c->sel, k.routed_scale, M, K, D, out, h, c->st));
+    ++c->launches;
+    return PC_OK;
+}
+
+// One full step over M rows already staged in d_tok / d_pos with sequence
+// slots `seq`.  lm_mode as in dense_jobs; nsplit_full = attention splits for
+// full-attention layers.
+pc_status run_step(pc_ctx *c, int M, const int *seq, int lm_mode, int nsplit_full, DenseJobs *dj) {
+    const pc_model_cfg &k = c->cfg;
+    const int D = k.hidden, H = k.n_heads, KVH = k.n_kv_heads, hd = k.head_dim;
+    PC_CU(launch_embed(c->emb_fmt, c->emb, c->emb_s, c->emb_gs, k.vocab, D, c->d_tok, M, c->h, c->st));
+    ++c->launches;
+    const int last = M - 1;
+    trace_row(c, "embedding", c->h + (size_t)last * D, D);
+    for (int l = 0; l < k.n_layers; ++l) {
+        Layer &ly = c->L[l];
+        const std::string pre = "layer" + std::to_string(l) + ".";
+        trace_row(c, pre + "input", c->h + (size_t)last * D, D);
+        PC_CU(launch_rmsnorm(c->h, ly.in_ln, c->hn, M, D, k.eps, c->st));
+        ++c->launches;
+        trace_row(c, pre + "pre_attn_norm", c->hn + (size_t)last * D, D);
+        void *kc = c->kc[l], *vc = c->vc[l];
+        if (ly.wq.t.fmt != TF_F32) {
+            GemvParams p{};
+            params_for(p, ly.wq.t, EPI_QKV);
+            p.jobs = dj->d_jobs + dj->qkv_off[l];
+            p.njobs = dj->d_counts + dj->qkv_cnt_idx[l];
+            p.x = c->hn;
+            p.ldx = D;
+            p.rope_cs = c->rope_cs;
+            p.rope_sn = c->rope_sn;
+            p.row_pos = c->d_pos;
+            p.row_seq = seq;
+            p.qbuf = c->qbuf;
+            p.ldq = H * hd;
+            p.kcache = kc;
+            p.vcache = vc;
+            p.kv_bf16 = c->opts.kv_bf16;
+            p.kv_seq_stride = c->seq_stride;
+            p.kv_ctx = c->kv_ctx;
+            p.kv_dim = KVH * hd;
+            PC_TRY(run_gemv(c, p, std::min(M, GEMV_MAXR), "qkv"));
+        } else {
+            const int Oq = H * hd, Ok = KVH * hd, ldr = Oq + 2 * Ok;
+            F32GemvParams f{};
+            f.I = D; f.x = c->hn; f.ldx = D; f.M = M; f.ldy = ldr;
+            f.W = ly.wq.t.f32; f.O = Oq; f.y = c->raw;
+            PC_CU(launch_gemv_f32(f, c->st));
+            f.W = ly.wk.t.f32; f.O = Ok; f.y = c->raw + Oq;
+            PC_CU(launch_gemv_f32(f, c->st));
+            f.W = ly.wv.t.f32; f.O = Ok; f.y = c->raw + Oq + Ok;
+            PC_CU(launch_gemv_f32(f, c->st));
+            QkvPostParams q{};
+            q.raw = c->raw; q.M = M; q.bq = ly.wq.bias; q.bk = ly.wk.bias; q.bv = ly.wv.bias;
+            q.H = H; q.KVH = KVH; q.hd = hd; q.rope_cs = c->rope_cs; q.rope_sn = c->rope_sn;
+            q.row_pos = c->d_pos; q.row_seq = seq; q.q = c->qbuf; q.kc = kc; q.vc = vc;
+            q.kv_bf16 = c->opts.kv_bf16; q.seq_stride = c->seq_stride; q.ctx = c->kv_ctx;
+            PC_CU(launch_qkv_post(q, c->st));
+            c->launches += 4;
+        }
+        trace_row(c, pre + "q_rope", c->qbuf + (size_t)last * H * hd, H * hd);
+        AttnParams a{};
+        a.q = c->qbuf; a.out = c->attn; a.kc = kc; a.vc = vc; a.kv_bf16 = c->opts.kv_bf16;
+        a.seq_stride = c->seq_stride; a.ctx = c->kv_ctx; a.sinks = ly.sinks; a.row_pos = c->d_pos;
+        a.row_seq = seq; a.M = M; a.H = H; a.KVH = KVH; a.hd = hd;
+        a.window = ly.layer_type == 0 ? k.sliding_window : 0;
+        a.part = c->attn_part; a.counter = c->attn_ctr;
+        a.nsplit = a.window > 0 ? std::max(1, std::min(c->attn_max_split, (a.window + ATTN_SPLIT - 1) / ATTN_SPLIT))
+                                : nsplit_full;
+        {
+            Prof pr(c, "attention");
+            PC_CU(launch_attention(a, c->st));
+        }
+        ++c->launches;
+        trace_row(c, pre + "attn_concat", c->attn + (size_t)last * H * hd, H * hd);
+        // o projection: + bias, + residual (picchio.c:615-616, 1691)
+        float *ydst = c->trace ? c->tmp : c->h;
+        if (ly.wo.t.fmt != TF_F32) {
+            GemvParams p{};
+            params_for(p, ly.wo.t, EPI_STORE);
+            p.jobs = dj->d_jobs + dj->o_off[l];
+            p.njobs = dj->d_counts + dj->o_cnt_idx[l];
+            p.x = c->attn;
+            p.ldx = H * hd;
+            p.y = ydst;
+            p.ldy = D;
+            p.residual = c->trace ? 0 : 1;
+            PC_TRY(run_gemv(c, p, std::min(M, GEMV_MAXR), "o_proj"));
+        } else {
+            F32GemvParams f{};
+            f.W = ly.wo.t.f32; f.O = D; f.I = H * hd; f.x = c->attn; f.ldx = H * hd; f.M = M;
+            f.bias = ly.wo.bias; f.y = ydst; f.ldy = D; f.residual = c->trace ? 0 : 1;
+            PC_CU(launch_gemv_f32(f, c->st));
+            ++c->launches;
+        }
+        if (c->trace) {
+            trace_row(c, pre + "attn_out", c->tmp + (size_t)last * D, D);
+            // residual add exactly as the fused epilogue does it (one fp32 add)
+            std::vector<float> hh((size_t)M * D), aa((size_t)M * D);
+            cudaStreamSynchronize(c->st);
+            cudaMemcpy(hh.data(), c->h, hh.size() * 4, cudaMemcpyDeviceToHost);
+            cudaMemcpy(aa.data(), c->tmp, aa.size() * 4, cudaMemcpyDeviceToHost);
+            for (size_t i = 0; i < hh.size(); ++i) hh[i] = hh[i] + aa[i];
+            cudaMemcpy(c->h, hh.data(), hh.size() * 4, cudaMemcpyHostToDevice);
+        }
+        trace_row(c, pre + "post_attn_residual", c->h + (size_t)last * D, D);
+        PC_CU(launch_rmsnorm(c->h, ly.post_ln, c->hn, M, D, k.eps, c->st));
+        ++c->launches;
+        trace_row(c, pre + "pre_moe_norm", c->hn + (size_t)last * D, D);
+        PC_TRY(run_moe(c, l, c->hn, M, nullptr, nullptr, 0, c->trace ? c->moe_out : nullptr, c->h));
+        trace_row(c, pre + "moe_out", c->moe_out + (size_t)last * D, D);
+        trace_row(c, pre + "output", c->h + (size_t)last * D, D);
+    }
+    PC_CU(launch_rmsnorm(c->h, c->final_norm, c->hn, M, D, k.eps, c->st));
+    ++c->launches;
+    trace_row(c, "final_norm", c->hn + (size_t)last * D, D);
+    if (lm_mode == 2) return PC_OK;
+    const int nlog = lm_mode == 1 ? 1 : M;
+    if (c->lm_head.t.fmt != TF_F32) {
+        GemvParams p{};
+        params_for(p, c->lm_head.t, EPI_LOGITS);
+        p.jobs = dj->d_jobs + dj->lm_off;
+        p.njobs = dj->d_counts + dj->lm_cnt_idx;
+        p.x = c->hn;
+        p.ldx = D;
+        p.y = c->logits;
+        p.ldy = k.vocab;
+        p.argmax = c->argmax;
+        PC_TRY(run_gemv(c, p, std::min(M, GEMV_MAXR), "lm_head"));
+    } else {
+        F32GemvParams f{};
+        f.W = c->lm_head.t.f32; f.O = k.vocab; f.I = D; f.x = c->hn + (size_t)(lm_mode == 1 ? M - 1 : 0) * D;
+        f.ldx = D; f.M = nlog; f.y = c->logits; f.ldy = k.vocab;
+        PC_CU(launch_gemv_f32(f, c->st));
+        PC_CU(launch_argmax_rows(c->logits, nlog, k.vocab, c->argmax, c->st));
+        c->launches += 2;
+    }
+    trace_row(c, "logits", c->logits + (size_t)(nlog - 1) * k.vocab, k.vocab);
+    PC_CU(launch_argmax_finish(c->argmax, nlog, c->d_next, nullptr, c->st));
+    ++c->launches;
+    return PC_OK;
+}
+
+int split_bucket(const pc_ctx *c, int max_pos) {
+    int n = (std::min(max_pos, c->kv_ctx - 1) + 1 + ATTN_SPLIT - 1) / ATTN_SPLIT;
+    int b = 1;
+    while (b < n) b <<= 1;
+    return std::min(b, c->attn_max_split);
+}
+
+pc_status check_err(pc_ctx *c) {
+    if (*c->h_err) {
+        *c->h_err = 0;
+        cudaMemsetAsync(c->err, 0, 4, c->st);
+        return fail(PC_ERR_TIMEOUT, "a device-side bounded wait gave up (GEMV pipeline)");
+    }
+    return PC_OK;
+}
+
+// Decode-shaped step (tokens/positions in h_tok/h_pos, M rows, KV slot =
+// row for batches, 0 for a single sequence): graph replay when enabled.
+pc_status decode_step(pc_ctx *c, int M, int *next) {
+    int maxp = 0;
+    for (int i = 0; i < M; ++i) maxp = std::max(maxp, c->h_pos[i]);
+    const int ns = split_bucket(c, maxp);
+    const int *seq = c->d_seq_rows;
+    DenseJobs *dj = nullptr;
+    PC_TRY(dense_jobs(c, M, 0, &dj));  // before any capture: it allocates
+    auto body = [&]() -> pc_status {
+        PC_CU(cudaMemcpyAsync(c->d_tok, c->h_tok, (size_t)M * 4, cudaMemcpyHostToDevice, c->st));
+        PC_CU(cudaMemcpyAsync(c->d_pos, c->h_pos, (size_t)M * 4, cudaMemcpyHostToDevice, c->st));
+        PC_TRY(run_step(c, M, seq, 0, ns, dj));
+        PC_CU(cudaMemcpyAsync(c->h_next, c->d_next, (size_t)(M) * 4, cudaMemcpyDeviceToHost, c->st));
+        PC_CU(cudaMemcpyAsync(c->h_err, c->err, 4, cudaMemcpyDeviceToHost, c->st));
+        return PC_OK;
+    };
+    if (c->opts.use_graphs && !c->trace) {
+        const uint64_t key = ((uint64_t)M << 20) | (uint64_t)ns;
+        auto it = c->graphs.find(key);
+        if (it == c->graphs.end()) {
+            cudaGraph_t g = nullptr;
+            const uint64_t before = c->launches;
+            PC_CU(cudaStreamBeginCapture(c->st, cudaStreamCaptureModeThreadLocal));
+            pc_status s = body();
+            cudaError_t e = cudaStreamEndCapture(c->st, &g);
+            const uint64_t per_step = c->launches - before;
+            c->launches = before;  // counted per replay below
+            if (s != PC_OK) { if (g) cudaGraphDestroy(g); return s; }
+            if (e != cudaSuccess) return cuda_fail(e, "cudaStreamEndCapture");
+            cudaGraphExec_t ex = nullptr;
+            e = cudaGraphInstantiate(&ex, g, 0);
+            cudaGraphDestroy(g);
+            if (e != cudaSuccess) return cuda_fail(e, "cudaGraphInstantiate");
+            it = c->graphs.emplace(key, StepGraph{ex, per_step}).first;
+        }
+        PC_CU(cudaGraphLaunch(it->second.exec, c->st));
+        c->launches += it->second.launches;
+    } else {
+        PC_TRY(body());
+    }
+    PC_CU(cudaStreamSynchronize(c->st));
+    PC_TRY(check_err(c));
+    for (int i = 0; i < M; ++i) next[i] = c->h_next[i];
+    return PC_OK;
+}
+
+pc_status check_ctx(pc_ctx *c) {
+    if (!c) return fail(PC_ERR_INVALID_ARG, "null context");
+    cudaError_t e = cudaSetDevice(c->dev);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaSetDevice");
+    return PC_OK;
+}
+
+pc_status make_ctx(const pc_opts *opts, pc_ctx **out) {
+    if (!out) return fail(PC_ERR_INVALID_ARG, "null output pointer");
+    *out = nullptr;
+    pc_ctx *c = new pc_ctx();
+    if (opts) c->opts = *opts;
+    else pc_default_opts(&c->opts);
+    c->dev = c->opts.device;
+    pc_status s = configure_device(c);
+    if (s != PC_OK) { delete c; return s; }
+    cudaError_t e = cudaStreamCreateWithFlags(&c->st, cudaStreamNonBlocking);
+    if (e != cudaSuccess) { delete c; return cuda_fail(e, "cudaStreamCreate"); }
+    *out = c;
+    return PC_OK;
+}
+
+pc_status finish_init(pc_ctx *c) {
+    if (c->opts.ep_size > 1) PC_TRY(ep_init(c));
+    return PC_OK;
+}
+
+void expert_range(pc_ctx *c) {
+    const int E = c->cfg.n_experts;
+    const int n = c->opts.ep_size > 1 ? c->opts.ep_size : 1, r = c->opts.ep_size > 1 ? c->opts.ep_rank : 0;
+    c->e_lo = (int)((int64_t)E * r / n);
+    c->e_hi = (int)((int64_t)E * (r + 1) / n);
+}
+
+}  // namespace
+}  // namespace pc
+
+using namespace pc;
+
+extern "C" {
+
+void pc_default_opts(pc_opts *o) {
+    if (!o) return;
+    memset(o, 0, sizeof *o);
+    o->device = 0;
+    o->ctx_len = 512;
+    o->kv_bf16 = 0;
+    o->max_batch = 1;
+    o->ep_size = 1;
+    o->use_graphs = 1;
+}
+
+const char *pc_status_string(pc_status s) {
+    switch (s) {
+        case PC_OK: return "PC_OK";
+        case PC_ERR_INVALID_ARG: return "PC_ERR_INVALID_ARG";
+        case PC_ERR_IO: return "PC_ERR_IO";
+        case PC_ERR_FORMAT: return "PC_ERR_FORMAT";
+        case PC_ERR_MISSING_TENSOR: return "PC_ERR_MISSING_TENSOR";
+        case PC_ERR_CUDA: return "PC_ERR_CUDA";
+        case PC_ERR_OOM: return "PC_ERR_OOM";
+        case PC_ERR_RANGE: return "PC_ERR_RANGE";
+        case PC_ERR_TIMEOUT: return "PC_ERR_TIMEOUT";
+        case PC_ERR_NCCL: return "PC_ERR_NCCL";
+        case PC_ERR_STATE: return "PC_ERR_STATE";
+    }
+    return "PC_ERR_UNKNOWN";
+}
+
+const char *pc_last_error(void) { return g_last_error.c_str(); }
+
+pc_status pc_init(const char *model_dir, const pc_opts *opts, pc_ctx **out) {
+    if (!model_dir) return fail(PC_ERR_INVALID_ARG, "null model_dir");
+    pc_ctx *c = nullptr;
+    PC_TRY(make_ctx(opts, &c));
+    std::string err;
+    // the expert range needs the config first
+    pc_status s = PC_OK;
+    if (!load_config(model_dir, &c->cfg, &err)) s = fail(PC_ERR_IO, err);
+    else expert_range(c);
+    if (s == PC_OK) s = load_model(c, model_dir);
+    if (s == PC_OK) s = finish_init(c);
+    if (s != PC_OK) { pc_free(c); return s; }
+    *out = c;
+    return PC_OK;
+}
+
+pc_status pc_init_synthetic(const pc_model_cfg *cfg, uint64_t seed, const pc_opts *opts, pc_ctx **out) {
+    if (!cfg) return fail(PC_ERR_INVALID_ARG, "null cfg");
+    pc_ctx *c = nullptr;
+    PC_TRY(make_ctx(opts, &c));
+    c->cfg = *cfg;
+    if (c->cfg.swiglu_alpha == 0.0f) c->cfg.swiglu_alpha = 1.702f;
+    if (c->cfg.routed_scale == 0.0f) c->cfg.routed_scale = 1.0f;
+    if (c->cfg.eps == 0.0f) c->cfg.eps = 1e-5f;
+    if (c->cfg.theta == 0.0f) c->cfg.theta = 150000.0f;
+    if (c->cfg.swiglu_limit == 0.0f) c->cfg.swiglu_limit = 7.0f;
+    if (c->cfg.ctx_len == 0) c->cfg.ctx_len = 131072;
+    if (c->cfg.rope_factor == 0.0f) c->cfg.rope_factor = 1.0f;
+    expert_range(c);
+    pc_status s = synth_model(c, seed);
+    if (s == PC_OK) s = finish_init(c);
+    if (s != PC_OK) { pc_free(c); return s; }
+    *out = c;
+    return PC_OK;
+}
+
+void pc_free(pc_ctx *c) {
+    if (!c) return;
+    cudaSetDevice(c->dev);
+    if (c->st) cudaStreamSynchronize(c->st);
+    for (auto &g : c->graphs) cudaGraphExecDestroy(g.second.exec);
+    c->graphs.clear();
+    ep_destroy(c);
+    for (void *p : c->allocs) cudaFree(p);
+    if (c->pinned) cudaFreeHost(c->pinned);
+    if (c->st) cudaStreamDestroy(c->st);
+    delete c;
+}
+
+pc_status pc_get_config(const pc_ctx *c, pc_model_cfg *cfg) {
+    if (!c || !cfg) return fail(PC_ERR_INVALID_ARG, "null argument");
+    *cfg = c->cfg;
+    return PC_OK;
+}
+
+pc_status pc_forward_token(pc_ctx *c, int tok, int pos, int *next_tok) {
+    PC_TRY(check_ctx(c));
+    if (!next_tok) return fail(PC_ERR_INVALID_ARG, "null next_tok");
+    if (pos < 0 || pos >= c->kv_ctx) return fail(PC_ERR_RANGE, "position " + std::to_string(pos) + " outside the KV capacity " + std::to_string(c->kv_ctx));
+    c->h_tok[0] = tok;
+    c->h_pos[0] = pos;
+    c->stages.clear();
+    return decode_step(c, 1, next_tok);
+}
+
+pc_status pc_decode_batch(pc_ctx *c, const int *toks, const int *pos, int B, int *next) {
+    PC_TRY(check_ctx(c));
+    if (!toks || !pos || !next) return fail(PC_ERR_INVALID_ARG, "null argument");
+    if (B < 1 || B > c->nseq || B > 256) return fail(PC_ERR_RANGE, "batch " + std::to_string(B) + " outside [1, max_batch]");
+    for (int i = 0; i < B; ++i) {
+        if (pos[i] < 0 || pos[i] >= c->kv_ctx) return fail(PC_ERR_RANGE, "position outside the KV capacity");
+        c->h_tok[i] = toks[i];
+        c->h_pos[i] = pos[i];
+    }
+    c->stages.clear();
+    return decode_step(c, B, next);
+}
+
+pc_status pc_prefill(pc_ctx *c, const int *ids, int n, int pos_base, int *next_tok) {
+    PC_TRY(check_ctx(c));
+    if (!ids || !next_tok || n < 1) return fail(PC_ERR_INVALID_ARG, "empty prompt");
+    if (pos_base < 0 || pos_base + n > c->kv_ctx) return fail(PC_ERR_RANGE, "prompt does not fit the KV capacity");
+    const int chunk = std::min(c->maxm, 64);
+    std::vector<int> tok(chunk), ps(chunk);
+    c->stages.clear();
+    for (int off = 0; off < n; off += chunk) {
+        const int m = std::min(chunk, n - off);
+        for (int i = 0; i < m; ++i) { tok[i] = ids[off + i]; ps[i] = pos_base + off + i; }
+        PC_CU(cudaMemcpyAsync(c->d_tok, tok.data(), (size_t)m * 4, cudaMemcpyHostToDevice, c->st));
+        PC_CU(cudaMemcpyAsync(c->d_pos, ps.data(), (size_t)m * 4, cudaMemcpyHostToDevice, c->st));
+        const bool last = off + m >= n;
+        DenseJobs *dj = nullptr;
+        PC_TRY(dense_jobs(c, m, last ? 1 : 2, &dj));
+        PC_TRY(run_step(c, m, c->d_seq_zero, last ? 1 : 2, split_bucket(c, ps[m - 1]), dj));
+        PC_CU(cudaStreamSynchronize(c->st));
+    }
+    PC_CU(cudaMemcpy(c->h_next, c->d_next, 4, cudaMemcpyDeviceToHost));
+    PC_CU(cudaMemcpy(c->h_err, c->err, 4, cudaMemcpyDeviceToHost));
+    PC_TRY(check_err(c));
+    *next_tok = c->h_next[0];
+    return PC_OK;
+}
+
+pc_status pc_get_logits(pc_ctx *c, int row, float *logits, int n) {
+    PC_TRY(check_ctx(c));
+    if (!logits || row < 0 || row >= c->max_logit_rows || n > c->cfg.vocab) return fail(PC_ERR_INVALID_ARG, "bad logits request");
+    PC_CU(cudaStreamSynchronize(c->st));
+    PC_CU(cudaMemcpy(logits, c->logits + (size_t)row * c->cfg.vocab, (size_t)n * 4, cudaMemcpyDeviceToHost));
+    return PC_OK;
+}
+
+pc_status pc_moe_layer(pc_ctx *c, int layer, const float *x_dev, float *out_dev, int M) {
+    PC_TRY(check_ctx(c));
+    if (layer < 0 || layer >= c->cfg.n_layers || !x_dev || !out_dev) return fail(PC_ERR_INVALID_ARG, "bad moe_layer arguments");
+    if (M < 1 || M > c->maxm) return fail(PC_ERR_RANGE, "M outside [1, " + std::to_string(c->maxm) + "]");
+    PC_TRY(run_moe(c, layer, x_dev, M, nullptr, nullptr, 0, out_dev, nullptr));
+    PC_CU(cudaMemcpyAsync(c->h_err, c->err, 4, cudaMemcpyDeviceToHost, c->st));
+    PC_CU(cudaStreamSynchronize(c->st));
+    return check_err(c);
+}
+
+pc_status pc_moe_experts(pc_ctx *c, int layer, const float *x_dev, const int *sel_dev, const float *w_dev, int M,
+                         float *out_dev) {
+    PC_TRY(check_ctx(c));
+    if (layer < 0 || layer >= c->cfg.n_layers || !x_dev || !out_dev || !sel_dev || !w_dev)
+        return fail(PC_ERR_INVALID_ARG, "bad moe_experts arguments");
+    if (M < 1 || M > c->maxm) return fail(PC_ERR_RANGE, "M outside [1, " + std::to_string(c->maxm) + "]");
+    PC_TRY(run_moe(c, layer, x_dev, M, sel_dev, w_dev, 0, out_dev, nullptr));
+    PC_CU(cudaMemcpyAsync(c->h_err, c->err, 4, cudaMemcpyDeviceToHost, c->st));
+    PC_CU(cudaStreamSynchronize(c->st));
+    return check_err(c);
+}
+
+pc_status pc_set_trace(pc_ctx *c, int on) {
+    if (!c) return fail(PC_ERR_INVALID_ARG, "null context");
+    c->trace = on != 0;
+    return PC_OK;
+}
+
+pc_status pc_get_stage(pc_ctx *c, const char *name, float *out, int n) {
+    if (!c || !name || !out) return fail(PC_ERR_INVALID_ARG, "null argument");
+    auto it = c->stages.find(name);
+    if (it == c->stages.end()) return fail(PC_ERR_STATE, std::string("no stage named ") + name);
+    if (n != (int)it->second.size()) return fail(PC_ERR_INVALID_ARG, "stage size is " + std::to_string(it->second.size()));
+    memcpy(out, it->second.data(), (size_t)n * 4);
+    return PC_OK;
+}
+
+pc_status pc_dump(pc_ctx *c, const char *dir) {
+    if (!c || !dir) return fail(PC_ERR_INVALID_ARG, "null argument");
+    for (auto &kv : c->stages) {
+        // same .npy header as oracle_dump (picchio.c:206-242): '<f4', shape (1, 1, n)
+        std::string path = std::string(dir) + "/" + kv.first + ".npy";
+        FILE *f = fopen(path.c_str(), "wb");
+        if (!f) return fail(PC_ERR_IO, "cannot write " + path);
+        char header[512];
+        int hl = snprintf(header, sizeof header, "{'descr': '<f4', 'fortran_order': False, 'shape': (1, 1, %zu), }",
+                          kv.second.size());
+        int padded = hl + 1;
+        while ((10 + padded) % 16) ++padded;
+        memset(header + hl, ' ', (size_t)(padded - hl));
+        header[padded - 1] = '\n';
+        const unsigned char magic[8] = {0x93, 'N', 'U', 'M', 'P', 'Y', 1, 0};
+        uint16_t hlen = (uint16_t)padded;
+        fwrite(magic, 1, 8, f);
+        fwrite(&hlen, 2, 1, f);
+        fwrite(header, 1, (size_t)padded, f);
+        fwrite(kv.second.data(), 4, kv.second.size(), f);
+        fclose(f);
+    }
+    return PC_OK;
+}
+
+pc_status pc_expert_prefetch(pc_ctx *c, int layer, const int *eids, int n) {
+    if (!c) return fail(PC_ERR_INVALID_ARG, "null context");
+    (void)layer; (void)eids; (void)n;
+    // Every expert is resident in HBM in this build: nothing to fetch.
+    return PC_OK;
+}
+
+pc_status pc_check_device(pc_ctx *c) {
+    PC_TRY(check_ctx(c));
+    PC_CU(cudaStreamSynchronize(c->st));
+    PC_CU(cudaMemcpy(c->h_err, c->err, 4, cudaMemcpyDeviceToHost));
+    return check_err(c);
+}
+
+uint64_t pc_kernel_launches(const pc_ctx *c) { return c ? c->launches : 0; }
+
+}  // extern "C"

@@ -1,0 +1,140 @@
+// ptx.cuh - thin inline-PTX helpers for sm_100a: mbarriers, bulk copies,
+// f16 tensor-core MMA and the nibble/byte to f16 conversions the dequant
+// GEMV uses.
+#pragma once
+#include <cstdint>
+
+namespace pc {
+
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count)
+                 : "memory");
+}
+
+__device__ __forceinline__ void fence_mbar_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t *bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+                 "r"(bytes)
+                 : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Bounded wait: gives up after `limit` polls (each poll may suspend the
+// thread for a hardware-chosen interval) and returns false.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity, uint32_t limit) {
+    for (uint32_t i = 0; i < limit; ++i)
+        if (mbar_try_wait(bar, parity)) return true;
+    return false;
+}
+
+__device__ __forceinline__ uint64_t l2_evict_first_policy() {
+    uint64_t pol;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+    return pol;
+}
+
+// Bulk (non-tensor) global -> shared copy completing on an mbarrier.  No
+// multicast: each CTA fetches its own bytes.  dst/src 16-byte aligned,
+// bytes a multiple of 16.
+__device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar,
+                                         uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint "
+        "[%0], [%1], %2, [%3], %4;" ::"r"(smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
+        : "memory");
+}
+
+__device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
+// D = A(16x16 f16, row) * B(16x8 f16, col) + C, fp32 accumulate.
+__device__ __forceinline__ void mma_f16_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0,
+                                              uint32_t b1, const float (&c)[4]) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
+        "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%11,%12,%13};"
+        : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "f"(c[0]), "f"(c[1]),
+          "f"(c[2]), "f"(c[3]));
+}
+
+__device__ __forceinline__ uint32_t lop3_and_or(uint32_t a, uint32_t b, uint32_t c) {
+    uint32_t r;
+    asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(r) : "r"(a), "r"(b), "r"(c));  // (a & b) | c
+    return r;
+}
+
+__device__ __forceinline__ uint32_t hsub2_u32(uint32_t a, uint32_t b) {
+    uint32_t r;
+    asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+    return r;
+}
+
+__device__ __forceinline__ uint32_t hfma2_u32(uint32_t a, uint32_t b, uint32_t c) {
+    uint32_t r;
+    asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(c));
+    return r;
+}
+
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+    uint32_t r;
+    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(sel));
+    return r;
+}
+
+// One 32-bit word of a T4 tile = one lane's A fragment of one m16n8k16 step:
+// nibbles (bits 0-3, 16-19) -> reg0, (4-7, 20-23) -> reg1, (8-11, 24-27) ->
+// reg2, (12-15, 28-31) -> reg3.  Each nibble n becomes the exact f16 value
+// n - 8: OR-ing n into the mantissa of 1024.0 gives 1024 + n (or 1024 + 16n
+// for the upper nibble of a byte), from which 1032 is subtracted (or which is
+// scaled by 1/16 and offset by -72); all steps are exact in f16.
+__device__ __forceinline__ void dequant_i4_word(uint32_t w, uint32_t (&a)[4]) {
+    const uint32_t MAGIC = 0x64006400u;
+    uint32_t t0 = lop3_and_or(w, 0x000F000Fu, MAGIC);
+    uint32_t t1 = lop3_and_or(w, 0x00F000F0u, MAGIC);
+    uint32_t w8 = w >> 8;
+    uint32_t t2 = lop3_and_or(w8, 0x000F000Fu, MAGIC);
+    uint32_t t3 = lop3_and_or(w8, 0x00F000F0u, MAGIC);
+    a[0] = hsub2_u32(t0, 0x64086408u);                 // - 1032
+    a[1] = hfma2_u32(t1, 0x2C002C00u, 0xD480D480u);    // * 1/16 - 72
+    a[2] = hsub2_u32(t2, 0x64086408u);
+    a[3] = hfma2_u32(t3, 0x2C002C00u, 0xD480D480u);
+}
+
+// Two 32-bit words of a T8 tile = one lane's A fragment of one step: bytes
+// (0,1) -> reg0, (2,3) -> reg1 of the first word, same for the second word
+// -> reg2, reg3.  Signed byte b becomes f16 (1024 + (b ^ 0x80)) - 1152 = b.
+__device__ __forceinline__ void dequant_i8_words(uint32_t w0, uint32_t w1, uint32_t (&a)[4]) {
+    const uint32_t MAGIC = 0x64646464u;
+    uint32_t u0 = w0 ^ 0x80808080u, u1 = w1 ^ 0x80808080u;
+    a[0] = hsub2_u32(prmt(u0, MAGIC, 0x4140u), 0x64806480u);
+    a[1] = hsub2_u32(prmt(u0, MAGIC, 0x4342u), 0x64806480u);
+    a[2] = hsub2_u32(prmt(u1, MAGIC, 0x4140u), 0x64806480u);
+    a[3] = hsub2_u32(prmt(u1, MAGIC, 0x4342u), 0x64806480u);
+}
+
+}  // namespace pc

@@ -1,0 +1,163 @@
+// qt.cu - the weight-level operator of the C ABI: one QT matrix uploaded
+// from the reference's host layout (quant.h:32-41) and applied with the
+// streaming GEMV, matmul_qt (quant.h:323-337).
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstring>
+#include <map>
+#include <string>
+#include <vector>
+
+#include "context.h"
+#include "gemv.h"
+#include "kernels.h"
+
+struct pc_qt {
+    int dev = 0, nsm = 148, max_smem = 0;
+    pc::TileDesc t;
+    std::vector<void *> allocs;
+    std::map<int, std::pair<pc::GemvJob *, int *>> jobs;  // per row count S
+    int *err = nullptr;
+};
+
+namespace {
+
+using namespace pc;
+
+pc_status qalloc(pc_qt *w, size_t bytes, void **out) {
+    cudaError_t e = cudaMalloc(out, bytes ? bytes : 16);
+    if (e != cudaSuccess) return fail(PC_ERR_OOM, std::string("cudaMalloc: ") + cudaGetErrorString(e));
+    w->allocs.push_back(*out);
+    return cudaMemset(*out, 0, bytes ? bytes : 16) == cudaSuccess ? PC_OK : fail(PC_ERR_CUDA, "cudaMemset");
+}
+
+pc_status jobs_for(pc_qt *w, int S, std::pair<GemvJob *, int *> &out) {
+    auto it = w->jobs.find(S);
+    if (it != w->jobs.end()) { out = it->second; return PC_OK; }
+    std::vector<GemvJob> jobs;
+    for (int r0 = 0; r0 < S; r0 += GEMV_MAXR) {
+        GemvJob j;
+        memset(&j, 0, sizeof j);
+        j.tiles = w->t.tiles;
+        j.rs = w->t.rs;
+        j.n_rt = w->t.Op / 16;
+        j.O = w->t.O;
+        j.nrows = std::min(GEMV_MAXR, S - r0);
+        for (int i = 0; i < j.nrows; ++i) j.in_row[i] = j.out_row[i] = r0 + i;
+        jobs.push_back(j);
+    }
+    GemvJob *dj = nullptr;
+    int *dc = nullptr;
+    PC_TRY(qalloc(w, jobs.size() * sizeof(GemvJob), (void **)&dj));
+    PC_TRY(qalloc(w, 4, (void **)&dc));
+    const int n = (int)jobs.size();
+    PC_CU(cudaMemcpy(dj, jobs.data(), jobs.size() * sizeof(GemvJob), cudaMemcpyHostToDevice));
+    PC_CU(cudaMemcpy(dc, &n, 4, cudaMemcpyHostToDevice));
+    out = {dj, dc};
+    w->jobs[S] = out;
+    return PC_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+pc_status pc_qt_create(int device, int fmt, int O, int I, int block_size, const void *data, const float *scales,
+                       pc_qt **out) {
+    if (!out || !data || O <= 0 || I <= 0) return fail(PC_ERR_INVALID_ARG, "bad pc_qt_create arguments");
+    if (fmt != PC_FMT_F32 && !scales) return fail(PC_ERR_INVALID_ARG, "quantized weights need scales");
+    if (fmt == PC_FMT_INT4 && block_size != 0 && block_size != 16 && block_size != 32 && block_size != 64)
+        return fail(PC_ERR_FORMAT, "INT4 block size must be 0, 16, 32 or 64");
+    pc_qt *w = new pc_qt();
+    w->dev = device;
+    pc_status s = device_setup(device, &w->nsm, &w->max_smem);
+    if (s != PC_OK) { delete w; return s; }
+    auto done = [&](pc_status st) { if (st != PC_OK) pc_qt_free(w); else *out = w; return st; };
+    s = qalloc(w, 4, (void **)&w->err);
+    if (s != PC_OK) return done(s);
+    if (fmt == PC_FMT_F32) {
+        tile_geom(w->t, TF_F32, O, I, 0, PERM_NONE, 0);
+        if ((s = qalloc(w, (size_t)O * I * 4, (void **)&w->t.f32)) != PC_OK) return done(s);
+        if (cudaMemcpy(w->t.f32, data, (size_t)O * I * 4, cudaMemcpyHostToDevice) != cudaSuccess)
+            return done(fail(PC_ERR_CUDA, "upload"));
+        return done(PC_OK);
+    }
+    const bool i4 = fmt == PC_FMT_INT4;
+    if (!i4 && fmt != PC_FMT_INT8) return done(fail(PC_ERR_FORMAT, "unknown format"));
+    tile_geom(w->t, i4 ? TF_T4 : TF_T8, O, I, i4 ? block_size : 0, PERM_NONE, 0);
+    if ((s = qalloc(w, (size_t)tile_bytes(w->t), (void **)&w->t.tiles)) != PC_OK) return done(s);
+    if (!i4 || block_size == 0)
+        if ((s = qalloc(w, (size_t)w->t.Op * 4, (void **)&w->t.rs)) != PC_OK) return done(s);
+    const int64_t qbytes = i4 ? (int64_t)O * ((I + 1) / 2) : (int64_t)O * I;
+    const int64_t ns = (i4 && block_size) ? (int64_t)O * ((I + block_size - 1) / block_size) : O;
+    void *dq = nullptr, *ds = nullptr;
+    if (cudaMalloc(&dq, qbytes) != cudaSuccess || cudaMalloc(&ds, ns * 4) != cudaSuccess)
+        return done(fail(PC_ERR_OOM, "staging"));
+    cudaMemcpy(dq, data, qbytes, cudaMemcpyHostToDevice);
+    cudaMemcpy(ds, scales, ns * 4, cudaMemcpyHostToDevice);
+    cudaError_t e = i4 ? retile_t4((const uint8_t *)dq, (const float *)ds, block_size, w->t, 0)
+                       : retile_t8((const int8_t *)dq, (const float *)ds, w->t, 0);
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    cudaFree(dq);
+    cudaFree(ds);
+    if (e != cudaSuccess) return done(cuda_fail(e, "retile"));
+    return done(PC_OK);
+}
+
+pc_status pc_qt_matmul(pc_qt *w, const float *x_dev, float *y_dev, int S, void *stream) {
+    if (!w || !x_dev || !y_dev || S < 1) return fail(PC_ERR_INVALID_ARG, "bad pc_qt_matmul arguments");
+    PC_CU(cudaSetDevice(w->dev));
+    cudaStream_t st = (cudaStream_t)stream;
+    if (w->t.fmt == TF_F32) {
+        F32GemvParams f{};
+        f.W = w->t.f32; f.O = w->t.O; f.I = w->t.I; f.x = x_dev; f.ldx = w->t.I; f.M = S;
+        f.y = y_dev; f.ldy = w->t.O;
+        PC_CU(launch_gemv_f32(f, st));
+        return PC_OK;
+    }
+    std::pair<GemvJob *, int *> j;
+    PC_TRY(jobs_for(w, S, j));
+    GemvParams p{};
+    p.jobs = j.first;
+    p.njobs = j.second;
+    p.fmt = w->t.fmt;
+    p.gs = w->t.gs;
+    p.kblocks = w->t.kblocks;
+    p.blk_bytes = w->t.blk_bytes;
+    p.I = w->t.I;
+    p.Ip = w->t.Ip;
+    p.perm = PERM_NONE;
+    p.epi = EPI_STORE;
+    p.x = x_dev;
+    p.ldx = w->t.I;
+    p.y = y_dev;
+    p.ldy = w->t.O;
+    p.err = w->err;
+    const int nt = std::min(S, GEMV_MAXR) <= 4 ? 1 : 2;
+    if (!gemv_plan(p, nt, w->max_smem)) return fail(PC_ERR_FORMAT, "input rows do not fit in shared memory");
+    PC_CU(gemv_launch(p, nt, w->nsm, st));
+    return PC_OK;
+}
+
+pc_status pc_qt_dequant(pc_qt *w, float *out_dev, void *stream) {
+    if (!w || !out_dev) return fail(PC_ERR_INVALID_ARG, "bad pc_qt_dequant arguments");
+    PC_CU(cudaSetDevice(w->dev));
+    if (w->t.fmt == TF_F32) {
+        PC_CU(cudaMemcpyAsync(out_dev, w->t.f32, (size_t)w->t.O * w->t.I * 4, cudaMemcpyDeviceToDevice,
+                              (cudaStream_t)stream));
+        return PC_OK;
+    }
+    PC_CU(dequant_tiles(w->t, out_dev, (cudaStream_t)stream));
+    return PC_OK;
+}
+
+void pc_qt_free(pc_qt *w) {
+    if (!w) return;
+    cudaSetDevice(w->dev);
+    cudaDeviceSynchronize();
+    for (void *p : w->allocs) cudaFree(p);
+    delete w;
+}
+
+}  // extern "C"
