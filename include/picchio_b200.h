@@ -124,6 +124,19 @@ pc_status pc_prefill(pc_ctx *ctx, const int *ids, int n, int pos_base, int *next
  * batched-decode form of forward_token.  B <= opts.max_batch. */
 pc_status pc_decode_batch(pc_ctx *ctx, const int *toks, const int *pos, int B, int *next);
 
+/* Greedy decode of n steps of one sequence without host round trips: the
+ * decode loop of picchio's main (picchio.c:3212-3287) at TEMPERATURE=0.
+ * Step i feeds the id of step i-1 (tok for i = 0) at position pos + i;
+ * out_ids[i] receives its greedy next id.  *device_ms (optional) receives
+ * the device time of the n steps, from CUDA events on the context stream. */
+pc_status pc_generate(pc_ctx *ctx, int tok, int pos, int n, int *out_ids, float *device_ms);
+
+/* Fills positions [0, n_pos) of sequence `seq`'s KV cache in every layer with
+ * seeded N(0, 1) values, standing in for a prompt of n_pos tokens when only
+ * the decode that follows is measured (no reference counterpart: the
+ * reference fills its KV cache only through prefill_tokens). */
+pc_status pc_kv_fill_synthetic(pc_ctx *ctx, int seq, int n_pos, uint64_t seed);
+
 /* Copies the logits of the last step (row `row` of a batch) to the host. */
 pc_status pc_get_logits(pc_ctx *ctx, int row, float *logits, int n);
 
@@ -179,6 +192,16 @@ pc_status pc_check_device(pc_ctx *ctx);
 
 /* Counts kernels this library launched on the context (for measurement). */
 uint64_t pc_kernel_launches(const pc_ctx *ctx);
+
+/* Kernel timing: between begin and end, steps run without CUDA graphs and
+ * every hot-path launch is bracketed by CUDA events on the context stream;
+ * pc_profile_get returns the summed duration and launch count of one label
+ * ("expert_gate_up", "expert_down", "qkv", "o_proj", "lm_head",
+ * "attention", "router").  Replaces the reference's t_attn / t_moe / t_head
+ * wall-clock accumulators (picchio.c:1686-1747). */
+pc_status pc_profile_begin(pc_ctx *ctx);
+pc_status pc_profile_end(pc_ctx *ctx);
+pc_status pc_profile_get(pc_ctx *ctx, const char *label, double *total_ms, int *count);
 
 #ifdef __cplusplus
 }

@@ -68,3 +68,54 @@ REF_API float ref_yarn_inv_freq(int head_dim, float theta, float factor, float b
     c.rope_truncate = truncate;
     return yarn_inv_freq(&c, j);
 }
+
+/* expert_apply (picchio.c:1769-1791) on one expert given as buffers in the
+ * reference's host layout: gate_up + bias + clamped SwiGLU + down + bias,
+ * dst += w * out. */
+REF_API void ref_expert_apply(const uint8_t *gu_q, const float *gu_s, int gu_bs, const float *gu_b,
+                              const uint8_t *dn_q, const float *dn_s, int dn_bs, const float *dn_b,
+                              int D, int I2, const float *x, float *dst, float w, float limit) {
+    Cfg c;
+    memset(&c, 0, sizeof(c));
+    c.hidden = D;
+    c.moe_inter = I2;
+    c.swiglu_limit = limit;
+    c.swiglu_alpha = 1.702f;
+    ESlot es;
+    memset(&es, 0, sizeof(es));
+    es.gu.fmt = 2; es.gu.O = I2; es.gu.I = D; es.gu.q4 = (uint8_t *)gu_q; es.gu.s = (float *)gu_s;
+    es.gu.block_size = gu_bs;
+    es.d.fmt = 2; es.d.O = D; es.d.I = I2 / 2; es.d.q4 = (uint8_t *)dn_q; es.d.s = (float *)dn_s;
+    es.d.block_size = dn_bs;
+    es.gu_bias = (float *)gu_b;
+    es.d_bias = (float *)dn_b;
+    expert_apply(&es, x, dst, w, &c);
+}
+
+/* gqa_attention (picchio.c:504-623) for one layer with INT8 projections and
+ * an fp32 KV cache of max_pos positions: projections, bias, RoPE, KV store,
+ * scores with sinks and window, P.V, output projection. */
+REF_API void ref_gqa_attention(const int8_t *wq, const float *sq, const int8_t *wk, const float *sk,
+                               const int8_t *wv, const float *sv, const int8_t *wo, const float *so,
+                               const float *bq, const float *bk, const float *bv, const float *bo,
+                               const float *sinks, float *Kc, float *Vc, int max_pos, int layer_type,
+                               int window, int pos, const float *x, float *out, int D, int H, int KVH,
+                               int hd, float theta) {
+    Cfg c;
+    memset(&c, 0, sizeof(c));
+    c.hidden = D; c.n_heads = H; c.n_kv_heads = KVH; c.head_dim = hd; c.sliding_window = window;
+    c.theta = theta; c.rope_factor = 1.0f; c.rope_attn_factor = 1.0f;
+    Layer ly;
+    memset(&ly, 0, sizeof(ly));
+    ly.wq.fmt = 1; ly.wq.O = H * hd; ly.wq.I = D; ly.wq.q8 = (int8_t *)wq; ly.wq.s = (float *)sq;
+    ly.wk.fmt = 1; ly.wk.O = KVH * hd; ly.wk.I = D; ly.wk.q8 = (int8_t *)wk; ly.wk.s = (float *)sk;
+    ly.wv.fmt = 1; ly.wv.O = KVH * hd; ly.wv.I = D; ly.wv.q8 = (int8_t *)wv; ly.wv.s = (float *)sv;
+    ly.wo.fmt = 1; ly.wo.O = D; ly.wo.I = H * hd; ly.wo.q8 = (int8_t *)wo; ly.wo.s = (float *)so;
+    ly.bq = (float *)bq; ly.bk = (float *)bk; ly.bv = (float *)bv; ly.bo = (float *)bo;
+    ly.sinks = (float *)sinks;
+    ly.layer_type = layer_type;
+    float *Kp[1] = {Kc}, *Vp[1] = {Vc};
+    KVCache kv;
+    kv.K = Kp; kv.V = Vp; kv.max_pos = max_pos; kv.cur_pos = 0;
+    gqa_attention(out, x, &ly, &kv, 0, pos, &c);
+}

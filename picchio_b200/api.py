@@ -141,6 +141,14 @@ def lib():
         L.pc_check_device.argtypes = [vp]
         L.pc_kernel_launches.argtypes = [vp]
         L.pc_kernel_launches.restype = C.c_uint64
+        L.pc_generate.argtypes = [vp, C.c_int, C.c_int, C.c_int, ip, fp]
+        L.pc_kv_fill_synthetic.argtypes = [vp, C.c_int, C.c_int, C.c_uint64]
+        L.pc_kv_fill_synthetic.restype = st
+        L.pc_profile_begin.argtypes = [vp]
+        L.pc_profile_end.argtypes = [vp]
+        L.pc_profile_get.argtypes = [vp, C.c_char_p, C.POINTER(C.c_double), ip]
+        for name in ("pc_generate", "pc_profile_begin", "pc_profile_end", "pc_profile_get"):
+            getattr(L, name).restype = st
         for name in ("pc_init", "pc_init_synthetic", "pc_get_config", "pc_forward_token", "pc_prefill",
                      "pc_decode_batch", "pc_get_logits", "pc_moe_layer", "pc_moe_experts", "pc_set_trace",
                      "pc_get_stage", "pc_dump", "pc_expert_prefetch", "pc_qt_create", "pc_qt_matmul",
@@ -245,6 +253,30 @@ class Model:
             tok = self.forward_token(tok, pos)
             pos += 1
         return out
+
+    def generate_device(self, tok: int, pos: int, n: int):
+        """n greedy steps on the device (pc_generate): returns (ids, device_ms)."""
+        out = (C.c_int * n)()
+        ms = C.c_float()
+        _check(lib().pc_generate(self._h, int(tok), int(pos), int(n), out, C.byref(ms)))
+        return list(out), float(ms.value)
+
+    def kv_fill_synthetic(self, n_pos: int, seq: int = 0, seed: int = 99):
+        _check(lib().pc_kv_fill_synthetic(self._h, seq, n_pos, seed))
+
+    def profile_begin(self):
+        _check(lib().pc_profile_begin(self._h))
+
+    def profile_end(self) -> dict:
+        """Ends profiling; returns {label: (total_ms, launches)}."""
+        _check(lib().pc_profile_end(self._h))
+        res = {}
+        for lab in ("expert_gate_up", "expert_down", "qkv", "o_proj", "lm_head", "attention", "router"):
+            t, n = C.c_double(), C.c_int()
+            _check(lib().pc_profile_get(self._h, lab.encode(), C.byref(t), C.byref(n)))
+            if n.value:
+                res[lab] = (t.value, n.value)
+        return res
 
     def logits(self, row: int = 0) -> np.ndarray:
         v = np.empty(self.config["vocab"], np.float32)

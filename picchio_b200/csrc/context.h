@@ -41,6 +41,8 @@ struct DenseJobs {
     std::vector<int> qkv_off, o_off;  // per layer: offset into d_jobs / index into d_counts
     std::vector<int> qkv_cnt_idx, o_cnt_idx;
     int lm_off = 0, lm_cnt_idx = 0;
+    std::vector<GemvJob> h_jobs;  // host copies, for launches that carry their jobs inline
+    std::vector<int> h_counts;
 };
 
 struct StepGraph {

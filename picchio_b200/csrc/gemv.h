@@ -6,8 +6,9 @@
 
 namespace pc {
 
-constexpr int GEMV_CONSUMERS = 8;
-constexpr int GEMV_THREADS = 32 * (GEMV_CONSUMERS + 1);
+constexpr int GEMV_CONSUMERS = 12;
+constexpr int GEMV_STEP_BLOCKS = 4;  // k-blocks a warp holds in registers per step
+constexpr int GEMV_THREADS = 32 * GEMV_CONSUMERS;
 
 size_t gemv_smem_bytes(int nt, int Ip, int stages, int stage_bytes);
 cudaError_t gemv_configure(int max_smem);

@@ -10,6 +10,7 @@
 #include <cfloat>
 
 #include "kernels.h"
+#include "launch.cuh"
 
 namespace pc {
 
@@ -30,6 +31,8 @@ __device__ __forceinline__ void stf(void *base, int64_t i, float v, int bf16) {
 // ---------------------------------------------------------------- embed ----
 __global__ void embed_kernel(int fmt, const void *table, const float *scales, int gs, int V, int D,
                              const int *tok, float *h) {
+    pdl_wait();
+    pdl_trigger();
     const int m = blockIdx.x;
     const int t = tok[m];
     float *out = h + (int64_t)m * D;
@@ -58,6 +61,8 @@ __global__ void embed_kernel(int fmt, const void *table, const float *scales, in
 
 // -------------------------------------------------------------- rmsnorm ----
 __global__ void rmsnorm_kernel(const float *x, const float *w, float *out, int D, float eps) {
+    pdl_wait();
+    pdl_trigger();
     __shared__ double red[32];
     const int m = blockIdx.x;
     const float *xr = x + (int64_t)m * D;
@@ -77,127 +82,10 @@ __global__ void rmsnorm_kernel(const float *x, const float *w, float *out, int D
     for (int i = threadIdx.x; i < D; i += blockDim.x) o[i] = __fmul_rn(__fmul_rn(xr[i], r), w[i]);
 }
 
-// ------------------------------------------------------------ attention ----
-// grid (nsplit, KVH, M), ATTN_SPLIT threads: thread t owns position
-// start + split*ATTN_SPLIT + t and computes its scores for every query head of
-// the KV group with the reference's sequential dot (picchio.c:571-575).
-constexpr int MAXG = 16, MAXHD = 128;
-
-__global__ void __launch_bounds__(ATTN_SPLIT) attention_kernel(const AttnParams a) {
-    __shared__ float qs[MAXG][MAXHD];
-    __shared__ float ps[MAXG][ATTN_SPLIT];
-    __shared__ float wred[MAXG][ATTN_SPLIT / 32];
-    __shared__ float mloc[MAXG], lloc[MAXG];
-    __shared__ bool last;
-    const int s = blockIdx.x, kh = blockIdx.y, m = blockIdx.z;
-    const int G = a.H / a.KVH, hd = a.hd, kvd = a.KVH * hd;
-    const int pos = a.row_pos[m];
-    int end = pos;
-    if (end >= a.ctx) end = a.ctx - 1;  // picchio.c:559-560
-    int start = 0;
-    if (a.window > 0) {
-        start = end - a.window + 1;
-        if (start < 0) start = 0;
-    }
-    const int p0 = start + s * ATTN_SPLIT;
-    const int cnt = max(0, min(ATTN_SPLIT, end + 1 - p0));
-    const int64_t cache0 = (int64_t)a.row_seq[m] * a.seq_stride + kh * hd;
-    for (int i = threadIdx.x; i < G * hd; i += blockDim.x)
-        qs[i / hd][i % hd] = a.q[(int64_t)m * a.H * hd + (kh * G) * hd + i];
-    __syncthreads();
-    const float scale = __fdiv_rn(1.0f, sqrtf((float)hd));
-    const int t = threadIdx.x;
-    if (t < cnt) {
-        const int64_t kb = cache0 + (int64_t)(p0 + t) * kvd;
-        float dot[MAXG];
-#pragma unroll
-        for (int g = 0; g < MAXG; ++g) dot[g] = 0.0f;
-        for (int i = 0; i < hd; ++i) {
-            const float kv = ldf(a.kc, kb + i, a.kv_bf16);
-#pragma unroll
-            for (int g = 0; g < MAXG; ++g)
-                if (g < G) dot[g] = __fadd_rn(dot[g], __fmul_rn(qs[g][i], kv));
-        }
-#pragma unroll
-        for (int g = 0; g < MAXG; ++g)
-            if (g < G) ps[g][t] = __fmul_rn(dot[g], scale);
-    }
-    // local max per head over this split's positions
-    const int warp = t >> 5, lane = t & 31;
-    for (int g = 0; g < G; ++g) {
-        float v = t < cnt ? ps[g][t] : -INFINITY;
-        for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
-        if (lane == 0) wred[g][warp] = v;
-    }
-    __syncthreads();
-    if (t < G) {
-        float v = -INFINITY;
-        for (int w = 0; w < ATTN_SPLIT / 32; ++w) v = fmaxf(v, wred[t][w]);
-        mloc[t] = v;
-    }
-    __syncthreads();
-    for (int g = 0; g < G; ++g) {
-        float e = 0.0f;
-        if (t < cnt) {
-            e = expf(__fsub_rn(ps[g][t], mloc[g]));
-            ps[g][t] = e;
-        }
-        for (int o = 16; o > 0; o >>= 1) e = __fadd_rn(e, __shfl_xor_sync(0xffffffffu, e, o));
-        if (lane == 0) wred[g][warp] = e;
-    }
-    __syncthreads();
-    if (t < G) {
-        float v = 0.0f;
-        for (int w = 0; w < ATTN_SPLIT / 32; ++w) v = __fadd_rn(v, wred[t][w]);
-        lloc[t] = v;
-    }
-    __syncthreads();
-    // P.V for (g, d) pairs; partial record: [m, l, o[hd]]
-    const int stride = hd + 2;
-    for (int idx = t; idx < G * hd; idx += blockDim.x) {
-        const int g = idx / hd, d = idx % hd;
-        float acc = 0.0f;
-        for (int u = 0; u < cnt; ++u)
-            acc = __fmaf_rn(ps[g][u], ldf(a.vc, cache0 + (int64_t)(p0 + u) * kvd + d, a.kv_bf16), acc);
-        float *rec = a.part + (((int64_t)m * a.H + kh * G + g) * a.nsplit + s) * stride;
-        rec[2 + d] = acc;
-        if (d == 0) {
-            rec[0] = cnt > 0 ? mloc[g] : -INFINITY;
-            rec[1] = cnt > 0 ? lloc[g] : 0.0f;
-        }
-    }
-    __threadfence();
-    __syncthreads();
-    if (t == 0) {
-        unsigned *c = a.counter + m * a.KVH + kh;
-        last = atomicAdd(c, 1u) == (unsigned)(a.nsplit - 1);
-        if (last) *c = 0u;
-    }
-    __syncthreads();
-    if (!last) return;
-    __threadfence();
-    // merge splits with the sink: the sink joins the max and the denominator
-    // only (picchio.c:586-596)
-    for (int idx = t; idx < G * hd; idx += blockDim.x) {
-        const int g = idx / hd, d = idx % hd, h = kh * G + g;
-        const float *rec0 = a.part + (((int64_t)m * a.H + h) * a.nsplit) * stride;
-        float M = a.sinks ? a.sinks[h] : -INFINITY;
-        for (int k = 0; k < a.nsplit; ++k) M = fmaxf(M, __ldcg(rec0 + k * stride));
-        float L = a.sinks ? expf(__fsub_rn(a.sinks[h], M)) : 0.0f;
-        float O = 0.0f;
-        for (int k = 0; k < a.nsplit; ++k) {
-            const float mk = __ldcg(rec0 + k * stride), lk = __ldcg(rec0 + k * stride + 1);
-            if (lk == 0.0f) continue;
-            const float f = expf(__fsub_rn(mk, M));
-            L = __fmaf_rn(lk, f, L);
-            O = __fmaf_rn(__ldcg(rec0 + k * stride + 2 + d), f, O);
-        }
-        a.out[(int64_t)m * a.H * hd + h * hd + d] = __fdiv_rn(O, L);
-    }
-}
-
 // --------------------------------------------------------------- router ----
 __global__ void __launch_bounds__(256) router_kernel(const RouterParams r) {
+    pdl_wait();
+    pdl_trigger();
     __shared__ bool last;
     __shared__ int cnt[256], jstart[257];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -205,10 +93,36 @@ __global__ void __launch_bounds__(256) router_kernel(const RouterParams r) {
         const int e = blockIdx.x * 8 + warp;
         if (e < r.E) {
             const float *re = r.R + (int64_t)e * r.D;
+            const bool vec = (r.D & 3) == 0;
             for (int m = 0; m < r.M; ++m) {
                 const float *xr = r.x + (int64_t)m * r.D;
                 float s = 0.0f;
-                for (int i = lane; i < r.D; i += 32) s = __fmaf_rn(xr[i], re[i], s);
+                if (vec) {
+                    // 16-byte loads, 8 in flight per lane, 4 partial sums
+                    const float4 *r4 = reinterpret_cast<const float4 *>(re);
+                    const float4 *x4 = reinterpret_cast<const float4 *>(xr);
+                    const int n4 = r.D >> 2;
+                    float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+                    for (int i0 = lane; i0 < n4; i0 += 32 * 8) {
+                        float4 rv[8], xv[8];
+#pragma unroll
+                        for (int j = 0; j < 8; ++j) {
+                            const int i = i0 + 32 * j;
+                            rv[j] = i < n4 ? r4[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+                            xv[j] = i < n4 ? x4[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+                        }
+#pragma unroll
+                        for (int j = 0; j < 8; ++j) {
+                            s0 = __fmaf_rn(xv[j].x, rv[j].x, s0);
+                            s1 = __fmaf_rn(xv[j].y, rv[j].y, s1);
+                            s2 = __fmaf_rn(xv[j].z, rv[j].z, s2);
+                            s3 = __fmaf_rn(xv[j].w, rv[j].w, s3);
+                        }
+                    }
+                    s = __fadd_rn(__fadd_rn(s0, s1), __fadd_rn(s2, s3));
+                } else {
+                    for (int i = lane; i < r.D; i += 32) s = __fmaf_rn(xr[i], re[i], s);
+                }
                 for (int o = 16; o > 0; o >>= 1) s = __fadd_rn(s, __shfl_xor_sync(0xffffffffu, s, o));
                 if (lane == 0) {
                     // decode adds the bias after the dot, prefill starts from it;
@@ -284,11 +198,23 @@ __global__ void __launch_bounds__(256) router_kernel(const RouterParams r) {
     }
     cnt[e] = (n + GEMV_MAXR - 1) / GEMV_MAXR;
     __syncthreads();
-    if (threadIdx.x == 0) {
-        int run = 0;
-        for (int i = 0; i < 256; ++i) { jstart[i] = run; run += cnt[i]; }
-        jstart[256] = run;
-        r.njobs[0] = r.njobs[1] = min(run, GEMV_MAX_JOBS);
+    if (warp == 0) {  // exclusive scan of jobs per expert: 8 experts per lane
+        int v[8], tot = 0;
+#pragma unroll
+        for (int q = 0; q < 8; ++q) { v[q] = tot; tot += cnt[lane * 8 + q]; }
+        int inc = tot;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int n = __shfl_up_sync(0xffffffffu, inc, o);
+            if (lane >= o) inc += n;
+        }
+        const int base = inc - tot;
+#pragma unroll
+        for (int q = 0; q < 8; ++q) jstart[lane * 8 + q] = base + v[q];
+        if (lane == 31) {
+            jstart[256] = inc;
+            r.njobs[0] = r.njobs[1] = min(inc, GEMV_MAX_JOBS);
+        }
     }
     __syncthreads();
     for (int p = threadIdx.x; p < P; p += blockDim.x) {
@@ -326,6 +252,8 @@ __global__ void __launch_bounds__(256) router_kernel(const RouterParams r) {
 // -------------------------------------------------------------- combine ----
 __global__ void combine_kernel(const float *eo, const float *w, const int *sel, float scale, int K,
                                int D, float *out, float *h) {
+    pdl_wait();
+    pdl_trigger();
     const int m = blockIdx.x;
     for (int i = threadIdx.x; i < D; i += blockDim.x) {
         float acc = 0.0f;
@@ -341,6 +269,8 @@ __global__ void combine_kernel(const float *eo, const float *w, const int *sel, 
 
 // ------------------------------------------------------------- f32 gemv ----
 __global__ void gemv_f32_kernel(const F32GemvParams p) {
+    pdl_wait();
+    pdl_trigger();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int o = blockIdx.x * 8 + warp;
     if (o >= p.O) return;
@@ -359,6 +289,8 @@ __global__ void gemv_f32_kernel(const F32GemvParams p) {
 }
 
 __global__ void qkv_post_kernel(const QkvPostParams p) {
+    pdl_wait();
+    pdl_trigger();
     const int m = blockIdx.y;
     const int half = p.hd / 2, Oq = p.H * p.hd, Ok = p.KVH * p.hd;
     const float *raw = p.raw + (int64_t)m * (Oq + 2 * Ok);
@@ -396,6 +328,8 @@ __global__ void qkv_post_kernel(const QkvPostParams p) {
 }
 
 __global__ void argmax_rows_kernel(const float *logits, int V, unsigned long long *packed) {
+    pdl_wait();
+    pdl_trigger();
     const int m = blockIdx.y;
     unsigned long long best = 0ull;
     for (int o = blockIdx.x * blockDim.x + threadIdx.x; o < V; o += gridDim.x * blockDim.x) {
@@ -415,6 +349,8 @@ __global__ void argmax_rows_kernel(const float *logits, int V, unsigned long lon
 }
 
 __global__ void argmax_finish_kernel(unsigned long long *packed, int n, int *ids, int *ids2) {
+    pdl_wait();
+    pdl_trigger();
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= n) return;
     const unsigned long long v = packed[i];
@@ -428,55 +364,63 @@ __global__ void argmax_finish_kernel(unsigned long long *packed, int n, int *ids
 
 cudaError_t launch_embed(int fmt, const void *table, const float *scales, int gs, int V, int D,
                          const int *tok, int M, float *h, cudaStream_t st) {
-    embed_kernel<<<M, 256, 0, st>>>(fmt, table, scales, gs, V, D, tok, h);
+    return launch_k(embed_kernel, dim3(M), dim3(256), 0, st, fmt, table, scales, gs, V, D, tok, h);
     return cudaGetLastError();
 }
 
 cudaError_t launch_rmsnorm(const float *x, const float *w, float *out, int M, int D, float eps,
                            cudaStream_t st) {
-    rmsnorm_kernel<<<M, 256, 0, st>>>(x, w, out, D, eps);
+    return launch_k(rmsnorm_kernel, dim3(M), dim3(256), 0, st, x, w, out, D, eps);
     return cudaGetLastError();
 }
 
-cudaError_t launch_attention(const AttnParams &a, cudaStream_t st) {
-    if (a.H / a.KVH > MAXG || a.hd > MAXHD) return cudaErrorInvalidValue;
-    dim3 grid(a.nsplit, a.KVH, a.M);
-    attention_kernel<<<grid, ATTN_SPLIT, 0, st>>>(a);
-    return cudaGetLastError();
-}
 
 cudaError_t launch_router(const RouterParams &r, cudaStream_t st) {
     if (r.E > 256 || r.K > 16) return cudaErrorInvalidValue;
     const int blocks = r.sel_in ? 1 : (r.E + 7) / 8;
-    router_kernel<<<blocks, 256, 0, st>>>(r);
+    return launch_k(router_kernel, dim3(blocks), dim3(256), 0, st, r);
     return cudaGetLastError();
 }
 
 cudaError_t launch_combine(const float *eo, const float *w, const int *sel, float scale, int M, int K,
                            int D, float *out, float *h, cudaStream_t st) {
-    combine_kernel<<<M, 256, 0, st>>>(eo, w, sel, scale, K, D, out, h);
+    return launch_k(combine_kernel, dim3(M), dim3(256), 0, st, eo, w, sel, scale, K, D, out, h);
     return cudaGetLastError();
 }
 
 cudaError_t launch_gemv_f32(const F32GemvParams &p, cudaStream_t st) {
-    gemv_f32_kernel<<<(p.O + 7) / 8, 256, 0, st>>>(p);
+    return launch_k(gemv_f32_kernel, dim3((p.O + 7) / 8), dim3(256), 0, st, p);
     return cudaGetLastError();
 }
 
 cudaError_t launch_qkv_post(const QkvPostParams &p, cudaStream_t st) {
     dim3 grid(8, p.M);
-    qkv_post_kernel<<<grid, 256, 0, st>>>(p);
+    return launch_k(qkv_post_kernel, dim3(grid), dim3(256), 0, st, p);
     return cudaGetLastError();
 }
 
 cudaError_t launch_argmax_rows(const float *logits, int M, int V, unsigned long long *packed, cudaStream_t st) {
     dim3 grid(64, M);
-    argmax_rows_kernel<<<grid, 256, 0, st>>>(logits, V, packed);
+    return launch_k(argmax_rows_kernel, dim3(grid), dim3(256), 0, st, logits, V, packed);
+    return cudaGetLastError();
+}
+
+__global__ void gen_advance_kernel(const int *next, int *pos, int *gen, int *step) {
+    pdl_wait();
+    pdl_trigger();
+    const int s = *step;
+    gen[s] = next[0];
+    *step = s + 1;
+    pos[0] += 1;
+}
+
+cudaError_t launch_gen_advance(const int *next, int *pos, int *gen, int *step, cudaStream_t st) {
+    return launch_k(gen_advance_kernel, dim3(1), dim3(1), 0, st, next, pos, gen, step);
     return cudaGetLastError();
 }
 
 cudaError_t launch_argmax_finish(unsigned long long *packed, int n, int *ids, int *ids2, cudaStream_t st) {
-    argmax_finish_kernel<<<(n + 127) / 128, 128, 0, st>>>(packed, n, ids, ids2);
+    return launch_k(argmax_finish_kernel, dim3((n + 127) / 128), dim3(128), 0, st, packed, n, ids, ids2);
     return cudaGetLastError();
 }
 

@@ -105,6 +105,9 @@ cudaError_t launch_qkv_post(const QkvPostParams &p, cudaStream_t st);
 // Packed greedy argmax of fp32 logit rows (first maximum wins).
 cudaError_t launch_argmax_rows(const float *logits, int M, int V, unsigned long long *packed, cudaStream_t st);
 
+// On-device decode loop bookkeeping: gen[*step] = next[0]; ++*step; ++pos[0].
+cudaError_t launch_gen_advance(const int *next, int *pos, int *gen, int *step, cudaStream_t st);
+
 // Greedy ids from the packed argmax words (and re-arms them).
 cudaError_t launch_argmax_finish(unsigned long long *packed, int n, int *ids, int *ids2,
                                  cudaStream_t st);
@@ -127,5 +130,7 @@ cudaError_t gen_i4_rowmajor(uint8_t *q4, float *scales, int O, int I, int gs, ui
 cudaError_t gen_i8_rowmajor(int8_t *q8, float *scales, int O, int I, uint64_t seed, float std_,
                             cudaStream_t st);
 cudaError_t gen_f32(float *dst, int64_t n, uint64_t seed, float mean, float std_, cudaStream_t st);
+// N(0, 1) into n elements of a KV cache (fp32 or bf16) starting at element off.
+cudaError_t gen_kv(void *base, int64_t off, int64_t n, int bf16, uint64_t seed, cudaStream_t st);
 
 }  // namespace pc

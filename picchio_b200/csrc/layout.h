@@ -68,6 +68,7 @@ __host__ __device__ inline int tile_row_to_logical(int perm, int head_dim, int r
 
 constexpr int GEMV_MAXR = 8;       // B rows (input vectors) per job
 constexpr int GEMV_MAX_JOBS = 1024;
+constexpr int GEMV_INLINE_JOBS = 6;
 
 // One job = one weight matrix applied to up to 8 input rows.
 struct GemvJob {
@@ -120,6 +121,15 @@ struct GemvParams {
     int *err;               // device error word
     int stages;             // pipeline depth for this launch
     int stage_bytes;
+    int static_jobs;        // 1: the job table does not depend on earlier kernels
+    // Shared input rows: > 0 means the B operand holds input rows
+    // 0..shared_rows-1 for the whole launch (filled once per CTA) and a job's
+    // in_row[r] is the B column of its row r.  0: per-job B (in_row = x row).
+    int shared_rows;
+    // Job table carried in the launch itself (n_inline > 0): no global reads
+    // before the first weight copy.
+    int n_inline;
+    GemvJob ijobs[GEMV_INLINE_JOBS];
 };
 
 }  // namespace pc

@@ -308,8 +308,9 @@ pc_status check_shapes(const pc_model_cfg &k) {
         k.topk <= 0 || k.intermediate <= 0 || k.vocab <= 0)
         return fail(PC_ERR_FORMAT, "config: non-positive dimension");
     if (k.n_heads % k.n_kv_heads) return fail(PC_ERR_FORMAT, "config: heads not a multiple of kv heads");
-    if (k.head_dim % 16 || k.head_dim > 128) return fail(PC_ERR_FORMAT, "config: head_dim must be a multiple of 16, <= 128");
-    if (k.n_heads / k.n_kv_heads > 16) return fail(PC_ERR_FORMAT, "config: more than 16 query heads per kv head");
+    if (k.head_dim != 16 && k.head_dim != 32 && k.head_dim != 64)
+        return fail(PC_ERR_FORMAT, "config: head_dim must be 16, 32 or 64");
+    if (k.n_heads / k.n_kv_heads > 8) return fail(PC_ERR_FORMAT, "config: more than 8 query heads per kv head");
     if (k.n_experts > 256 || k.topk > 16 || k.topk > k.n_experts) return fail(PC_ERR_FORMAT, "config: experts <= 256, top-k <= 16");
     if (k.intermediate % 8) return fail(PC_ERR_FORMAT, "config: intermediate_size must be a multiple of 8");
     return PC_OK;
@@ -436,8 +437,13 @@ pc_status alloc_runtime(pc_ctx *c) {
     PC_TRY(dalloc(c, 16, (void **)&c->router_ctr));
     PC_TRY(dalloc(c, (size_t)M * KVH * 4, (void **)&c->attn_ctr));
     c->attn_max_split = (c->kv_ctx + 255) / 256;
+    if (c->attn_max_split > 64)  // the decode attention merges at most 64 spans of 256 positions
+        return fail(PC_ERR_RANGE, "ctx_len above 16384 positions is not supported");
     PC_TRY(dalloc(c, (size_t)M * H * c->attn_max_split * (hd + 2) * 4, (void **)&c->attn_part));
     PC_TRY(dalloc(c, (size_t)M * 8, (void **)&c->argmax));
+    c->gen_cap = c->kv_ctx;
+    PC_TRY(dalloc(c, (size_t)c->gen_cap * 4, (void **)&c->d_gen));
+    PC_TRY(dalloc(c, 16, (void **)&c->d_step));
     PC_CU(cudaMallocHost(&c->pinned, 4096));
     c->h_tok = (int *)c->pinned;
     c->h_pos = c->h_tok + 256;

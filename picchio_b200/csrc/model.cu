@@ -95,7 +95,7 @@ struct Prof {
 // Launch one GEMV over a device job list.
 pc_status run_gemv(pc_ctx *c, GemvParams p, int rows_per_job, const char *label) {
     p.err = c->err;
-    const int nt = nt_for_rows(rows_per_job);
+    const int nt = nt_for_rows(p.shared_rows > 0 ? p.shared_rows : rows_per_job);
     if (!gemv_plan(p, nt, c->max_smem))
         return fail(PC_ERR_FORMAT, "GEMV input of " + std::to_string(p.Ip) + " columns does not fit in shared memory");
     Prof pr(c, label);
@@ -114,6 +114,7 @@ void params_for(GemvParams &p, const TileDesc &t, int epi) {
     p.perm = t.perm;
     p.head_dim = t.head_dim;
     p.epi = epi;
+    p.static_jobs = 1;  // dense job tables are built on the host; MoE clears this
 }
 
 GemvJob make_job(const TileDesc &t, const float *bias, int seg, const int *in, const int *out, int n) {
@@ -190,10 +191,28 @@ pc_status dense_jobs(pc_ctx *c, int M, int lm_mode, DenseJobs **out) {
     PC_TRY(dalloc(c, counts.size() * 4, (void **)&dj.d_counts));
     PC_CU(cudaMemcpy(dj.d_jobs, jobs.data(), jobs.size() * sizeof(GemvJob), cudaMemcpyHostToDevice));
     PC_CU(cudaMemcpy(dj.d_counts, counts.data(), counts.size() * 4, cudaMemcpyHostToDevice));
+    dj.h_jobs = jobs;
+    dj.h_counts = counts;
     auto res = c->dense_jobs.emplace(key, dj);
     *out = &res.first->second;
     return PC_OK;
 }
+
+// Points a launch at job list `cnt_idx` (starting at `off`) of a dense table:
+// carried inline in the launch when it is short, else read from the device.
+void use_jobs(GemvParams &p, const DenseJobs *dj, int off, int cnt_idx) {
+    const int n = dj->h_counts[cnt_idx];
+    p.jobs = dj->d_jobs + off;
+    p.njobs = dj->d_counts + cnt_idx;
+    p.n_inline = 0;
+    if (n > 0 && n <= GEMV_INLINE_JOBS) {
+        p.n_inline = n;
+        for (int j = 0; j < n; ++j) p.ijobs[j] = dj->h_jobs[off + j];
+    }
+}
+
+// Launches with at most 8 input rows keep them all in the B operand.
+int shared_rows_for(int rows) { return rows <= GEMV_MAXR ? rows : 0; }
 
 void trace_row(pc_ctx *c, const std::string &name, const float *dev, int n) {
     if (!c->trace) return;
@@ -267,6 +286,7 @@ pc_status run_moe(pc_ctx *c, int l, const float *x, int M, const int *sel_in, co
     const int rows = std::min(M, GEMV_MAXR);
     GemvParams p{};
     params_for(p, c->eg.gu, EPI_SWIGLU);
+    p.static_jobs = 0;  // written by the router kernel
     p.jobs = c->jobs_gu;
     p.njobs = c->njobs;
     p.x = x;
@@ -275,16 +295,19 @@ pc_status run_moe(pc_ctx *c, int l, const float *x, int M, const int *sel_in, co
     p.ldy = k.intermediate;
     p.swiglu_limit = k.swiglu_limit;
     p.swiglu_alpha = k.swiglu_alpha;
+    p.shared_rows = shared_rows_for(M);  // B column = token row
     PC_TRY(run_gemv(c, p, rows, "expert_gate_up"));
     const bool ep = c->nccl_comm != nullptr;
     if (ep) PC_CU(cudaMemsetAsync(c->eo, 0, (size_t)M * K * D * 4, c->st));
     params_for(p, c->eg.dn, EPI_STORE);
+    p.static_jobs = 0;
     p.jobs = c->jobs_dn;
     p.njobs = c->njobs + 1;
     p.x = c->act;
     p.ldx = k.intermediate;
     p.y = c->eo;
     p.ldy = D;
+    p.shared_rows = shared_rows_for(M * K);  // B column = (token, k) pair
     PC_TRY(run_gemv(c, p, rows, "expert_down"));
     if (ep) PC_TRY(ep_allreduce_sum(c, c->eo, (size_t)M * K * D));
     if (c->trace) {
@@ -304,7 +327,8 @@ pc_status run_moe(pc_ctx *c, int l, const float *x, int M, const int *sel_in, co
 // One full step over M rows already staged in d_tok / d_pos with sequence
 // slots `seq`.  lm_mode as in dense_jobs; nsplit_full = attention splits for
 // full-attention layers.
-pc_status run_step(pc_ctx *c, int M, const int *seq, int lm_mode, int nsplit_full, DenseJobs *dj) {
+pc_status run_step(pc_ctx *c, int M, const int *seq, int lm_mode, int nsplit_full, DenseJobs *dj,
+                   bool feedback = false) {
     const pc_model_cfg &k = c->cfg;
     const int D = k.hidden, H = k.n_heads, KVH = k.n_kv_heads, hd = k.head_dim;
     PC_CU(launch_embed(c->emb_fmt, c->emb, c->emb_s, c->emb_gs, k.vocab, D, c->d_tok, M, c->h, c->st));
@@ -322,8 +346,8 @@ pc_status run_step(pc_ctx *c, int M, const int *seq, int lm_mode, int nsplit_ful
         if (ly.wq.t.fmt != TF_F32) {
             GemvParams p{};
             params_for(p, ly.wq.t, EPI_QKV);
-            p.jobs = dj->d_jobs + dj->qkv_off[l];
-            p.njobs = dj->d_counts + dj->qkv_cnt_idx[l];
+            use_jobs(p, dj, dj->qkv_off[l], dj->qkv_cnt_idx[l]);
+            p.shared_rows = shared_rows_for(M);
             p.x = c->hn;
             p.ldx = D;
             p.rope_cs = c->rope_cs;
@@ -377,8 +401,8 @@ pc_status run_step(pc_ctx *c, int M, const int *seq, int lm_mode, int nsplit_ful
         if (ly.wo.t.fmt != TF_F32) {
             GemvParams p{};
             params_for(p, ly.wo.t, EPI_STORE);
-            p.jobs = dj->d_jobs + dj->o_off[l];
-            p.njobs = dj->d_counts + dj->o_cnt_idx[l];
+            use_jobs(p, dj, dj->o_off[l], dj->o_cnt_idx[l]);
+            p.shared_rows = shared_rows_for(M);
             p.x = c->attn;
             p.ldx = H * hd;
             p.y = ydst;
@@ -418,8 +442,8 @@ pc_status run_step(pc_ctx *c, int M, const int *seq, int lm_mode, int nsplit_ful
     if (c->lm_head.t.fmt != TF_F32) {
         GemvParams p{};
         params_for(p, c->lm_head.t, EPI_LOGITS);
-        p.jobs = dj->d_jobs + dj->lm_off;
-        p.njobs = dj->d_counts + dj->lm_cnt_idx;
+        use_jobs(p, dj, dj->lm_off, dj->lm_cnt_idx);
+        p.shared_rows = shared_rows_for(M);
         p.x = c->hn;
         p.ldx = D;
         p.y = c->logits;
@@ -435,7 +459,11 @@ pc_status run_step(pc_ctx *c, int M, const int *seq, int lm_mode, int nsplit_ful
         c->launches += 2;
     }
     trace_row(c, "logits", c->logits + (size_t)(nlog - 1) * k.vocab, k.vocab);
-    PC_CU(launch_argmax_finish(c->argmax, nlog, c->d_next, nullptr, c->st));
+    PC_CU(launch_argmax_finish(c->argmax, nlog, c->d_next, feedback ? c->d_tok : nullptr, c->st));
+    ++c->launches;
+    if (feedback) {  // on-device loop: record the id, advance the position
+        PC_CU(launch_gen_advance(c->d_next, c->d_pos, c->d_gen, c->d_step, c->st));
+    }
     ++c->launches;
     return PC_OK;
 }
@@ -456,6 +484,34 @@ pc_status check_err(pc_ctx *c) {
     return PC_OK;
 }
 
+// Runs `body` on the context stream: captured once into a CUDA graph under
+// `key` and replayed afterwards, unless graphs are off or the step is traced
+// or profiled (those need host work between kernels).
+template <typename F>
+pc_status run_graph(pc_ctx *c, uint64_t key, F &&body) {
+    if (!c->opts.use_graphs || c->trace || c->prof) return body();
+    auto it = c->graphs.find(key);
+    if (it == c->graphs.end()) {
+        cudaGraph_t g = nullptr;
+        const uint64_t before = c->launches;
+        PC_CU(cudaStreamBeginCapture(c->st, cudaStreamCaptureModeThreadLocal));
+        pc_status s = body();
+        cudaError_t e = cudaStreamEndCapture(c->st, &g);
+        const uint64_t per_step = c->launches - before;
+        c->launches = before;  // counted per replay below
+        if (s != PC_OK) { if (g) cudaGraphDestroy(g); return s; }
+        if (e != cudaSuccess) return cuda_fail(e, "cudaStreamEndCapture");
+        cudaGraphExec_t ex = nullptr;
+        e = cudaGraphInstantiate(&ex, g, 0);
+        cudaGraphDestroy(g);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaGraphInstantiate");
+        it = c->graphs.emplace(key, StepGraph{ex, per_step}).first;
+    }
+    PC_CU(cudaGraphLaunch(it->second.exec, c->st));
+    c->launches += it->second.launches;
+    return PC_OK;
+}
+
 // Decode-shaped step (tokens/positions in h_tok/h_pos, M rows, KV slot =
 // row for batches, 0 for a single sequence): graph replay when enabled.
 pc_status decode_step(pc_ctx *c, int M, int *next) {
@@ -473,34 +529,41 @@ pc_status decode_step(pc_ctx *c, int M, int *next) {
         PC_CU(cudaMemcpyAsync(c->h_err, c->err, 4, cudaMemcpyDeviceToHost, c->st));
         return PC_OK;
     };
-    if (c->opts.use_graphs && !c->trace) {
-        const uint64_t key = ((uint64_t)M << 20) | (uint64_t)ns;
-        auto it = c->graphs.find(key);
-        if (it == c->graphs.end()) {
-            cudaGraph_t g = nullptr;
-            const uint64_t before = c->launches;
-            PC_CU(cudaStreamBeginCapture(c->st, cudaStreamCaptureModeThreadLocal));
-            pc_status s = body();
-            cudaError_t e = cudaStreamEndCapture(c->st, &g);
-            const uint64_t per_step = c->launches - before;
-            c->launches = before;  // counted per replay below
-            if (s != PC_OK) { if (g) cudaGraphDestroy(g); return s; }
-            if (e != cudaSuccess) return cuda_fail(e, "cudaStreamEndCapture");
-            cudaGraphExec_t ex = nullptr;
-            e = cudaGraphInstantiate(&ex, g, 0);
-            cudaGraphDestroy(g);
-            if (e != cudaSuccess) return cuda_fail(e, "cudaGraphInstantiate");
-            it = c->graphs.emplace(key, StepGraph{ex, per_step}).first;
-        }
-        PC_CU(cudaGraphLaunch(it->second.exec, c->st));
-        c->launches += it->second.launches;
-    } else {
-        PC_TRY(body());
-    }
+    PC_TRY(run_graph(c, ((uint64_t)M << 20) | (uint64_t)ns, body));
     PC_CU(cudaStreamSynchronize(c->st));
     PC_TRY(check_err(c));
     for (int i = 0; i < M; ++i) next[i] = c->h_next[i];
     return PC_OK;
+}
+
+// Greedy decode of one sequence entirely on the device: each step's argmax
+// becomes the next step's token without a host round trip (the decode loop
+// of picchio.c:3212-3287 at TEMPERATURE=0).
+pc_status generate(pc_ctx *c, int tok, int pos, int n, int *out, float *device_ms) {
+    const int ns = split_bucket(c, pos + n - 1);
+    DenseJobs *dj = nullptr;
+    PC_TRY(dense_jobs(c, 1, 0, &dj));
+    auto body = [&]() -> pc_status { return run_step(c, 1, c->d_seq_rows, 0, ns, dj, true); };
+    c->h_tok[0] = tok;
+    c->h_pos[0] = pos;
+    PC_CU(cudaMemcpyAsync(c->d_tok, c->h_tok, 4, cudaMemcpyHostToDevice, c->st));
+    PC_CU(cudaMemcpyAsync(c->d_pos, c->h_pos, 4, cudaMemcpyHostToDevice, c->st));
+    PC_CU(cudaMemsetAsync(c->d_step, 0, 4, c->st));
+    cudaEvent_t e0, e1;
+    PC_CU(cudaEventCreate(&e0));
+    PC_CU(cudaEventCreate(&e1));
+    PC_CU(cudaEventRecord(e0, c->st));
+    for (int i = 0; i < n; ++i) PC_TRY(run_graph(c, (1ull << 62) | (uint64_t)ns, body));
+    PC_CU(cudaEventRecord(e1, c->st));
+    PC_CU(cudaMemcpyAsync(out, c->d_gen, (size_t)n * 4, cudaMemcpyDeviceToHost, c->st));
+    PC_CU(cudaMemcpyAsync(c->h_err, c->err, 4, cudaMemcpyDeviceToHost, c->st));
+    PC_CU(cudaStreamSynchronize(c->st));
+    float ms = 0.0f;
+    cudaEventElapsedTime(&ms, e0, e1);
+    cudaEventDestroy(e0);
+    cudaEventDestroy(e1);
+    if (device_ms) *device_ms = ms;
+    return check_err(c);
 }
 
 pc_status check_ctx(pc_ctx *c) {
@@ -762,5 +825,62 @@ pc_status pc_check_device(pc_ctx *c) {
 }
 
 uint64_t pc_kernel_launches(const pc_ctx *c) { return c ? c->launches : 0; }
+
+pc_status pc_generate(pc_ctx *c, int tok, int pos, int n, int *out_ids, float *device_ms) {
+    PC_TRY(check_ctx(c));
+    if (!out_ids || n < 1) return fail(PC_ERR_INVALID_ARG, "bad pc_generate arguments");
+    if (pos < 0 || pos + n > c->kv_ctx) return fail(PC_ERR_RANGE, "decode does not fit the KV capacity");
+    c->stages.clear();
+    return generate(c, tok, pos, n, out_ids, device_ms);
+}
+
+pc_status pc_kv_fill_synthetic(pc_ctx *c, int seq, int n_pos, uint64_t seed) {
+    PC_TRY(check_ctx(c));
+    if (seq < 0 || seq >= c->nseq || n_pos < 0 || n_pos > c->kv_ctx) return fail(PC_ERR_RANGE, "bad KV range");
+    const int64_t n = (int64_t)n_pos * c->cfg.n_kv_heads * c->cfg.head_dim;
+    for (int l = 0; l < c->cfg.n_layers; ++l) {
+        for (int kv = 0; kv < 2; ++kv) {
+            void *base = kv ? c->vc[l] : c->kc[l];
+            const int64_t off = (int64_t)seq * c->seq_stride;
+            PC_CU(gen_kv(base, off, n, c->opts.kv_bf16, seed ^ (0x1000ull * l + kv), c->st));
+        }
+    }
+    PC_CU(cudaStreamSynchronize(c->st));
+    return PC_OK;
+}
+
+pc_status pc_profile_begin(pc_ctx *c) {
+    if (!c) return fail(PC_ERR_INVALID_ARG, "null context");
+    for (auto &e : c->prof_evs) { cudaEventDestroy(e.a); cudaEventDestroy(e.b); }
+    c->prof_evs.clear();
+    c->prof_acc.clear();
+    c->prof = true;
+    return PC_OK;
+}
+
+pc_status pc_profile_end(pc_ctx *c) {
+    PC_TRY(check_ctx(c));
+    PC_CU(cudaStreamSynchronize(c->st));
+    for (auto &e : c->prof_evs) {
+        float ms = 0.0f;
+        cudaEventElapsedTime(&ms, e.a, e.b);
+        auto &acc = c->prof_acc[e.label];
+        acc.first += ms;
+        acc.second += 1;
+        cudaEventDestroy(e.a);
+        cudaEventDestroy(e.b);
+    }
+    c->prof_evs.clear();
+    c->prof = false;
+    return PC_OK;
+}
+
+pc_status pc_profile_get(pc_ctx *c, const char *label, double *total_ms, int *count) {
+    if (!c || !label || !total_ms || !count) return fail(PC_ERR_INVALID_ARG, "null argument");
+    auto it = c->prof_acc.find(label);
+    *total_ms = it == c->prof_acc.end() ? 0.0 : it->second.first;
+    *count = it == c->prof_acc.end() ? 0 : it->second.second;
+    return PC_OK;
+}
 
 }  // extern "C"

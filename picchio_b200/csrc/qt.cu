@@ -129,6 +129,20 @@ pc_status pc_qt_matmul(pc_qt *w, const float *x_dev, float *y_dev, int S, void *
     p.Ip = w->t.Ip;
     p.perm = PERM_NONE;
     p.epi = EPI_STORE;
+    p.static_jobs = 1;
+    if (S <= GEMV_MAXR) {  // one job, carried in the launch; all rows in the B operand
+        GemvJob jb;
+        memset(&jb, 0, sizeof jb);
+        jb.tiles = w->t.tiles;
+        jb.rs = w->t.rs;
+        jb.n_rt = w->t.Op / 16;
+        jb.O = w->t.O;
+        jb.nrows = S;
+        for (int i = 0; i < S; ++i) jb.in_row[i] = jb.out_row[i] = i;
+        p.n_inline = 1;
+        p.ijobs[0] = jb;
+        p.shared_rows = S;
+    }
     p.x = x_dev;
     p.ldx = w->t.I;
     p.y = y_dev;

@@ -3,6 +3,8 @@
 // tile layout (layout.h), the inverse dequant view used by the tests, and
 // seeded synthetic weights quantized as the reference converter does
 // (convert.py:45-126).
+#include <cuda_bf16.h>
+
 #include <cstdint>
 
 #include "kernels.h"
@@ -202,6 +204,16 @@ __global__ void gen_f32_kernel(float *dst, int64_t n, uint64_t seed, float mean,
         dst[i] = __fadd_rn(mean, __fmul_rn(sd, normal_at(seed, (uint64_t)i)));
 }
 
+__global__ void gen_kv_kernel(void *base, int64_t off, int64_t n, int bf16, uint64_t seed) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        const float v = normal_at(seed, (uint64_t)i);
+        if (bf16)
+            reinterpret_cast<__nv_bfloat16 *>(base)[off + i] = __float2bfloat16_rn(v);
+        else
+            reinterpret_cast<float *>(base)[off + i] = v;
+    }
+}
+
 int grid_for(int64_t n, int threads) {
     int64_t b = (n + threads - 1) / threads;
     return (int)(b < 1 ? 1 : (b > 148 * 64 ? 148 * 64 : b));
@@ -237,6 +249,11 @@ cudaError_t gen_i4_rowmajor(uint8_t *q4, float *scales, int O, int I, int gs, ui
 
 cudaError_t gen_i8_rowmajor(int8_t *q8, float *scales, int O, int I, uint64_t seed, float sd, cudaStream_t st) {
     gen_i8_kernel<<<grid_for(O, 64), 64, 0, st>>>(q8, scales, O, I, seed, sd);
+    return cudaGetLastError();
+}
+
+cudaError_t gen_kv(void *base, int64_t off, int64_t n, int bf16, uint64_t seed, cudaStream_t st) {
+    gen_kv_kernel<<<grid_for(n, 256), 256, 0, st>>>(base, off, n, bf16, seed);
     return cudaGetLastError();
 }
 
