@@ -7,7 +7,10 @@
 namespace pc {
 
 constexpr int GEMV_CONSUMERS = 12;
-constexpr int GEMV_STEP_BLOCKS = 4;  // k-blocks a warp holds in registers per step
+// k-blocks a warp holds in registers per step (64-column T4 or 32-column T8 blocks)
+__host__ __device__ constexpr int gemv_step_blocks(int fmt) { return fmt == TF_T4 ? 4 : 8; }
+// N-tiles (8 MMA columns = 2 input rows x 4 digit columns) for a job of `rows` input rows
+inline int gemv_nt_for_rows(int rows) { return rows <= 2 ? 1 : rows <= 4 ? 2 : 4; }
 constexpr int GEMV_THREADS = 32 * GEMV_CONSUMERS;
 
 size_t gemv_smem_bytes(int nt, int Ip, int stages, int stage_bytes);

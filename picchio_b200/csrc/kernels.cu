@@ -60,59 +60,104 @@ __global__ void embed_kernel(int fmt, const void *table, const float *scales, in
 }
 
 // -------------------------------------------------------------- rmsnorm ----
-__global__ void rmsnorm_kernel(const float *x, const float *w, float *out, int D, float eps) {
+// One block per row.  On B200 an L2 round trip costs ~0.7 us, so every
+// thread issues all of its loads (x and w, 16 bytes each) before using any:
+// one round trip in, one out.
+constexpr int NORM_THREADS = 256, NORM_V4 = 4;  // up to 4 float4 per thread (D <= 4096)
+
+__global__ void __launch_bounds__(NORM_THREADS) rmsnorm_kernel(const float *x, const float *w, float *out, int D,
+                                                                float eps) {
     pdl_wait();
     pdl_trigger();
-    __shared__ double red[32];
-    const int m = blockIdx.x;
+    __shared__ double red[NORM_THREADS / 32];
+    __shared__ float rs;
+    const int m = blockIdx.x, tid = threadIdx.x;
     const float *xr = x + (int64_t)m * D;
+    float *o = out + (int64_t)m * D;
     double s = 0.0;
-    for (int i = threadIdx.x; i < D; i += blockDim.x) s += (double)xr[i] * (double)xr[i];
-    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = s;
+    const bool vec = (D & 3) == 0 && D <= 4 * NORM_V4 * NORM_THREADS;
+    float4 xv[NORM_V4], wv[NORM_V4];
+    if (vec) {
+        const int n4 = D >> 2;
+#pragma unroll
+        for (int j = 0; j < NORM_V4; ++j) {
+            const int i = tid + j * NORM_THREADS;
+            xv[j] = i < n4 ? reinterpret_cast<const float4 *>(xr)[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+            wv[j] = i < n4 ? reinterpret_cast<const float4 *>(w)[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+#pragma unroll
+        for (int j = 0; j < NORM_V4; ++j)
+            s += (double)xv[j].x * xv[j].x + (double)xv[j].y * xv[j].y + (double)xv[j].z * xv[j].z +
+                 (double)xv[j].w * xv[j].w;
+    } else {
+        for (int i = tid; i < D; i += NORM_THREADS) s += (double)xr[i] * (double)xr[i];
+    }
+    // sum of squares in double, as quant.h:396-402 accumulates it
+    for (int q = 16; q > 0; q >>= 1) s += __shfl_xor_sync(0xffffffffu, s, q);
+    if ((tid & 31) == 0) red[tid >> 5] = s;
     __syncthreads();
-    if (threadIdx.x < 32) {
-        double v = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.0;
-        for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-        if (threadIdx.x == 0) red[0] = v;
+    if (tid < 32) {
+        double v = tid < NORM_THREADS / 32 ? red[tid] : 0.0;
+        for (int q = 16; q > 0; q >>= 1) v += __shfl_xor_sync(0xffffffffu, v, q);
+        if (tid == 0) rs = __fdiv_rn(1.0f, sqrtf(__fadd_rn((float)(v / D), eps)));
     }
     __syncthreads();
-    const float r = __fdiv_rn(1.0f, sqrtf(__fadd_rn((float)(red[0] / D), eps)));
-    float *o = out + (int64_t)m * D;
-    for (int i = threadIdx.x; i < D; i += blockDim.x) o[i] = __fmul_rn(__fmul_rn(xr[i], r), w[i]);
+    const float r = rs;
+    if (vec) {
+        const int n4 = D >> 2;
+#pragma unroll
+        for (int j = 0; j < NORM_V4; ++j) {
+            const int i = tid + j * NORM_THREADS;
+            if (i < n4)
+                reinterpret_cast<float4 *>(o)[i] =
+                    make_float4(__fmul_rn(__fmul_rn(xv[j].x, r), wv[j].x), __fmul_rn(__fmul_rn(xv[j].y, r), wv[j].y),
+                                __fmul_rn(__fmul_rn(xv[j].z, r), wv[j].z), __fmul_rn(__fmul_rn(xv[j].w, r), wv[j].w));
+        }
+    } else {
+        for (int i = tid; i < D; i += NORM_THREADS) o[i] = __fmul_rn(__fmul_rn(xr[i], r), w[i]);
+    }
 }
 
 // --------------------------------------------------------------- router ----
+// Dot products: four warps per expert (two experts per block), each lane
+// with all of its 16-byte loads of R and x in flight at once; the quarters
+// are added in a fixed order.  The last block to finish (atomic ticket) does
+// the top-k, the softmax and the expert job tables, reading the selection
+// from shared memory.
+constexpr int ROUTER_RV = 6;  // float4 per lane per operand in flight
+
 __global__ void __launch_bounds__(256) router_kernel(const RouterParams r) {
     pdl_wait();
     pdl_trigger();
     __shared__ bool last;
+    __shared__ float part[8];
     __shared__ int cnt[256], jstart[257];
+    __shared__ int ssel[GEMV_MAX_JOBS];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int P = r.M * r.K;
     if (!r.sel_in) {
-        const int e = blockIdx.x * 8 + warp;
-        if (e < r.E) {
-            const float *re = r.R + (int64_t)e * r.D;
-            const bool vec = (r.D & 3) == 0;
-            for (int m = 0; m < r.M; ++m) {
+        const int e = blockIdx.x * 2 + (warp >> 2), q = warp & 3;
+        const bool vec = (r.D & 3) == 0;
+        for (int m = 0; m < r.M; ++m) {
+            float s = 0.0f;
+            if (e < r.E) {
+                const float *re = r.R + (int64_t)e * r.D;
                 const float *xr = r.x + (int64_t)m * r.D;
-                float s = 0.0f;
                 if (vec) {
-                    // 16-byte loads, 8 in flight per lane, 4 partial sums
+                    const int n4 = r.D >> 2, i0 = n4 * q / 4, i1 = n4 * (q + 1) / 4;
                     const float4 *r4 = reinterpret_cast<const float4 *>(re);
                     const float4 *x4 = reinterpret_cast<const float4 *>(xr);
-                    const int n4 = r.D >> 2;
                     float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
-                    for (int i0 = lane; i0 < n4; i0 += 32 * 8) {
-                        float4 rv[8], xv[8];
+                    for (int base = i0 + lane; base < i1; base += 32 * ROUTER_RV) {
+                        float4 rv[ROUTER_RV], xv[ROUTER_RV];
 #pragma unroll
-                        for (int j = 0; j < 8; ++j) {
-                            const int i = i0 + 32 * j;
-                            rv[j] = i < n4 ? r4[i] : make_float4(0.f, 0.f, 0.f, 0.f);
-                            xv[j] = i < n4 ? x4[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+                        for (int j = 0; j < ROUTER_RV; ++j) {
+                            const int i = base + 32 * j;
+                            rv[j] = i < i1 ? r4[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+                            xv[j] = i < i1 ? x4[i] : make_float4(0.f, 0.f, 0.f, 0.f);
                         }
 #pragma unroll
-                        for (int j = 0; j < 8; ++j) {
+                        for (int j = 0; j < ROUTER_RV; ++j) {
                             s0 = __fmaf_rn(xv[j].x, rv[j].x, s0);
                             s1 = __fmaf_rn(xv[j].y, rv[j].y, s1);
                             s2 = __fmaf_rn(xv[j].z, rv[j].z, s2);
@@ -121,19 +166,27 @@ __global__ void __launch_bounds__(256) router_kernel(const RouterParams r) {
                     }
                     s = __fadd_rn(__fadd_rn(s0, s1), __fadd_rn(s2, s3));
                 } else {
-                    for (int i = lane; i < r.D; i += 32) s = __fmaf_rn(xr[i], re[i], s);
-                }
-                for (int o = 16; o > 0; o >>= 1) s = __fadd_rn(s, __shfl_xor_sync(0xffffffffu, s, o));
-                if (lane == 0) {
-                    // decode adds the bias after the dot, prefill starts from it;
-                    // with a parallel dot both become one final add.
-                    if (r.bias) s = r.bias_first ? __fadd_rn(r.bias[e], s) : __fadd_rn(s, r.bias[e]);
-                    r.logits[(int64_t)m * r.E + e] = s;
+                    const int i0 = r.D * q / 4, i1 = r.D * (q + 1) / 4;
+                    for (int i = i0 + lane; i < i1; i += 32) s = __fmaf_rn(xr[i], re[i], s);
                 }
             }
+            for (int o = 16; o > 0; o >>= 1) s = __fadd_rn(s, __shfl_xor_sync(0xffffffffu, s, o));
+            if (lane == 0) part[warp] = s;
+            __syncthreads();
+            if (threadIdx.x < 2) {
+                const int ee = blockIdx.x * 2 + threadIdx.x;
+                if (ee < r.E) {
+                    const float *pp = part + 4 * threadIdx.x;
+                    float v = __fadd_rn(__fadd_rn(pp[0], pp[1]), __fadd_rn(pp[2], pp[3]));
+                    // decode adds the bias after the dot, prefill starts from it;
+                    // with a parallel dot both become one final add.
+                    if (r.bias) v = r.bias_first ? __fadd_rn(r.bias[ee], v) : __fadd_rn(v, r.bias[ee]);
+                    r.logits[(int64_t)m * r.E + ee] = v;
+                }
+            }
+            __syncthreads();
         }
         __threadfence();
-        __syncthreads();
         if (threadIdx.x == 0) {
             last = atomicAdd(r.counter, 1u) == gridDim.x - 1;
             if (last) *r.counter = 0u;
@@ -145,6 +198,7 @@ __global__ void __launch_bounds__(256) router_kernel(const RouterParams r) {
         for (int m = warp; m < r.M; m += 8) {
             const float *lg = r.logits + (int64_t)m * r.E;
             float vals[8];
+#pragma unroll
             for (int q = 0; q < 8; ++q) {
                 const int e = lane + 32 * q;
                 vals[q] = e < r.E ? __ldcg(lg + e) : -INFINITY;
@@ -154,6 +208,7 @@ __global__ void __launch_bounds__(256) router_kernel(const RouterParams r) {
             for (int k = 0; k < r.K; ++k) {
                 float bv = -1e30f;
                 int bi = -1;
+#pragma unroll
                 for (int q = 0; q < 8; ++q) {
                     const int e = lane + 32 * q;
                     if (e < r.E && vals[q] > bv) { bv = vals[q]; bi = e; }
@@ -163,9 +218,11 @@ __global__ void __launch_bounds__(256) router_kernel(const RouterParams r) {
                     const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
                     if (ov > bv || (ov == bv && oi >= 0 && (bi < 0 || oi < bi))) { bv = ov; bi = oi; }
                 }
-                sk[k] = bi;
-                wk[k] = bv;
-                if (bi >= 0 && (bi & 31) == lane) vals[bi >> 5] = -INFINITY;
+                sk[k < 16 ? k : 15] = bi;
+                wk[k < 16 ? k : 15] = bv;
+#pragma unroll
+                for (int q = 0; q < 8; ++q)
+                    if (bi >= 0 && bi == lane + 32 * q) vals[q] = -INFINITY;
             }
             if (lane == 0) {
                 // softmax over the K selected logits (quant.h:406-412)
@@ -175,26 +232,28 @@ __global__ void __launch_bounds__(256) router_kernel(const RouterParams r) {
                 for (int k = 0; k < r.K; ++k) { wk[k] = expf(__fsub_rn(wk[k], mx)); sum = __fadd_rn(sum, wk[k]); }
                 for (int k = 0; k < r.K; ++k) {
                     r.sel[m * r.K + k] = sk[k];
+                    if (m * r.K + k < GEMV_MAX_JOBS) ssel[m * r.K + k] = sk[k];
                     r.w[m * r.K + k] = __fdiv_rn(wk[k], sum);
                 }
             }
         }
         __syncthreads();
-        __threadfence_block();
     } else {
         if (blockIdx.x != 0) return;
-        for (int i = threadIdx.x; i < r.M * r.K; i += blockDim.x) {
-            r.sel[i] = r.sel_in[i];
+        for (int i = threadIdx.x; i < P; i += blockDim.x) {
+            const int v = r.sel_in[i];
+            r.sel[i] = v;
+            if (i < GEMV_MAX_JOBS) ssel[i] = v;
             r.w[i] = r.w_in[i];
         }
         __syncthreads();
     }
     // expert job tables: pairs grouped by expert, at most 8 pairs per job
-    const int P = r.M * r.K;
+    const int Ps = min(P, GEMV_MAX_JOBS);
     const int e = threadIdx.x;
     int n = 0;
     if (e < r.E && e >= r.e_lo && e < r.e_hi) {
-        for (int p = 0; p < P; ++p) n += (__ldcg(r.sel + p) == e);
+        for (int p = 0; p < Ps; ++p) n += (ssel[p] == e);
     }
     cnt[e] = (n + GEMV_MAXR - 1) / GEMV_MAXR;
     __syncthreads();
@@ -205,8 +264,8 @@ __global__ void __launch_bounds__(256) router_kernel(const RouterParams r) {
         int inc = tot;
 #pragma unroll
         for (int o = 1; o < 32; o <<= 1) {
-            const int n = __shfl_up_sync(0xffffffffu, inc, o);
-            if (lane >= o) inc += n;
+            const int nn = __shfl_up_sync(0xffffffffu, inc, o);
+            if (lane >= o) inc += nn;
         }
         const int base = inc - tot;
 #pragma unroll
@@ -217,16 +276,16 @@ __global__ void __launch_bounds__(256) router_kernel(const RouterParams r) {
         }
     }
     __syncthreads();
-    for (int p = threadIdx.x; p < P; p += blockDim.x) {
-        const int ep = __ldcg(r.sel + p);
+    for (int p = threadIdx.x; p < Ps; p += blockDim.x) {
+        const int ep = ssel[p];
         r.pair_local[p] = (ep >= r.e_lo && ep < r.e_hi) ? 1 : 0;
     }
     if (n == 0) return;
     const int slot = r.slot_of ? r.slot_of[e] : e - r.e_lo;
     const uint8_t *base = r.table + (int64_t)slot * r.stride;
     int j = jstart[e], fill = 0;
-    for (int p = 0; p < P && j < GEMV_MAX_JOBS; ++p) {
-        if (__ldcg(r.sel + p) != e) continue;
+    for (int p = 0; p < Ps && j < GEMV_MAX_JOBS; ++p) {
+        if (ssel[p] != e) continue;
         GemvJob &gu = r.jobs_gu[j];
         GemvJob &dn = r.jobs_dn[j];
         if (fill == 0) {
@@ -250,18 +309,73 @@ __global__ void __launch_bounds__(256) router_kernel(const RouterParams r) {
 }
 
 // -------------------------------------------------------------- combine ----
-__global__ void combine_kernel(const float *eo, const float *w, const int *sel, float scale, int K,
-                               int D, float *out, float *h) {
+// One block per row; expert rows are taken four at a time with all their
+// loads in flight.  The fma chain runs in k order, as picchio.c:1445-1454
+// accumulates it; a failed expert (sel < 0) is skipped (picchio.c:1394).
+__global__ void __launch_bounds__(NORM_THREADS) combine_kernel(const float *eo, const float *w, const int *sel,
+                                                                float scale, int K, int D, float *out, float *h) {
     pdl_wait();
     pdl_trigger();
-    const int m = blockIdx.x;
-    for (int i = threadIdx.x; i < D; i += blockDim.x) {
-        float acc = 0.0f;
-        for (int k = 0; k < K; ++k) {
-            if (sel && sel[m * K + k] < 0) continue;  // failed expert is skipped (picchio.c:1394)
-            const float wk = __fmul_rn(w[m * K + k], scale);
-            acc = __fmaf_rn(wk, eo[((int64_t)m * K + k) * D + i], acc);
+    const int m = blockIdx.x, tid = threadIdx.x;
+    float wk[16];
+    bool ok[16];
+#pragma unroll
+    for (int k = 0; k < 16; ++k) {
+        ok[k] = k < K && !(sel && sel[m * K + k] < 0);
+        wk[k] = k < K ? __fmul_rn(w[m * K + k], scale) : 0.0f;
+    }
+    const bool vec = (D & 3) == 0 && D <= 4 * 3 * NORM_THREADS;
+    if (vec) {
+        const int n4 = D >> 2;
+        float4 acc[3], hv[3];
+#pragma unroll
+        for (int j = 0; j < 3; ++j) {
+            acc[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+            const int i = tid + j * NORM_THREADS;
+            hv[j] = (h && i < n4) ? reinterpret_cast<const float4 *>(h + (int64_t)m * D)[i] : acc[j];
         }
+#pragma unroll
+        for (int k0 = 0; k0 < 16; k0 += 4) {
+            if (k0 >= K) break;
+            float4 e[4][3];
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk)
+#pragma unroll
+                for (int j = 0; j < 3; ++j) {
+                    const int i = tid + j * NORM_THREADS;
+                    e[kk][j] = (k0 + kk < K && i < n4)
+                                   ? reinterpret_cast<const float4 *>(eo + ((int64_t)m * K + k0 + kk) * D)[i]
+                                   : make_float4(0.f, 0.f, 0.f, 0.f);
+                }
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk) {
+                if (!ok[k0 + kk]) continue;
+                const float c = wk[k0 + kk];
+#pragma unroll
+                for (int j = 0; j < 3; ++j) {
+                    acc[j].x = __fmaf_rn(c, e[kk][j].x, acc[j].x);
+                    acc[j].y = __fmaf_rn(c, e[kk][j].y, acc[j].y);
+                    acc[j].z = __fmaf_rn(c, e[kk][j].z, acc[j].z);
+                    acc[j].w = __fmaf_rn(c, e[kk][j].w, acc[j].w);
+                }
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < 3; ++j) {
+            const int i = tid + j * NORM_THREADS;
+            if (i >= n4) continue;
+            if (out) reinterpret_cast<float4 *>(out + (int64_t)m * D)[i] = acc[j];
+            if (h)
+                reinterpret_cast<float4 *>(h + (int64_t)m * D)[i] =
+                    make_float4(__fadd_rn(hv[j].x, acc[j].x), __fadd_rn(hv[j].y, acc[j].y),
+                                __fadd_rn(hv[j].z, acc[j].z), __fadd_rn(hv[j].w, acc[j].w));
+        }
+        return;
+    }
+    for (int i = tid; i < D; i += NORM_THREADS) {
+        float acc = 0.0f;
+        for (int k = 0; k < K; ++k)
+            if (ok[k < 16 ? k : 15]) acc = __fmaf_rn(wk[k < 16 ? k : 15], eo[((int64_t)m * K + k) * D + i], acc);
         if (out) out[(int64_t)m * D + i] = acc;
         if (h) h[(int64_t)m * D + i] = __fadd_rn(h[(int64_t)m * D + i], acc);
     }
@@ -370,21 +484,21 @@ cudaError_t launch_embed(int fmt, const void *table, const float *scales, int gs
 
 cudaError_t launch_rmsnorm(const float *x, const float *w, float *out, int M, int D, float eps,
                            cudaStream_t st) {
-    return launch_k(rmsnorm_kernel, dim3(M), dim3(256), 0, st, x, w, out, D, eps);
+    return launch_k(rmsnorm_kernel, dim3(M), dim3(NORM_THREADS), 0, st, x, w, out, D, eps);
     return cudaGetLastError();
 }
 
 
 cudaError_t launch_router(const RouterParams &r, cudaStream_t st) {
-    if (r.E > 256 || r.K > 16) return cudaErrorInvalidValue;
-    const int blocks = r.sel_in ? 1 : (r.E + 7) / 8;
+    if (r.E > 256 || r.K > 16 || r.M * r.K > GEMV_MAX_JOBS) return cudaErrorInvalidValue;
+    const int blocks = r.sel_in ? 1 : (r.E + 1) / 2;
     return launch_k(router_kernel, dim3(blocks), dim3(256), 0, st, r);
     return cudaGetLastError();
 }
 
 cudaError_t launch_combine(const float *eo, const float *w, const int *sel, float scale, int M, int K,
                            int D, float *out, float *h, cudaStream_t st) {
-    return launch_k(combine_kernel, dim3(M), dim3(256), 0, st, eo, w, sel, scale, K, D, out, h);
+    return launch_k(combine_kernel, dim3(M), dim3(NORM_THREADS), 0, st, eo, w, sel, scale, K, D, out, h);
     return cudaGetLastError();
 }
 

@@ -6,19 +6,20 @@
 //
 //  T4 (INT4): the matrix is cut into row tiles of 16 rows; a row tile is a
 //   contiguous run of blocks, one block per 64 columns.  A block is 512 bytes
-//   of nibbles - 32 lanes x 16 bytes, where lane L = 4g + t holds, for each of
-//   the four 16-column MMA steps s, one 32-bit word with the 8 nibbles of its
-//   m16n8k16 A fragment (rows g and g+8, columns 2t, 2t+1, 2t+8, 2t+9) - then
-//   the group scales of the block: float[8 g][64/gs groups][row g, row g+8].
-//   Per-row scaled INT4 (block_size 0) has no scale bytes in the block and a
-//   separate float[O] row-scale array instead.
-//  T8 (INT8): same 16-row tiles, blocks of 32 columns = 512 bytes (two MMA
-//   steps, 8 bytes per lane each), plus a float[O] row-scale array.
+//   of nibbles - 32 lanes x 16 bytes, where lane L = 4g + t holds its A
+//   fragments of the two m16n8k32 s8 MMA steps of the block: word 2m + h
+//   has, in byte j, column 32m + 16h + 4t + j of row g (low nibble) and of
+//   row g + 8 (high nibble) - then the group scales of the block:
+//   float[8 g][64/gs groups][row g, row g+8].  Per-row scaled INT4
+//   (block_size 0) has no scale bytes in the block and a separate float[O]
+//   row-scale array instead.
+//  T8 (INT8): same 16-row tiles, blocks of 32 columns = 512 bytes, one
+//   m16n8k32 step: word 2h + r of lane 4g + t has columns 16h + 4t + j of
+//   row g (r = 0) or g + 8 (r = 1); plus a float[O] row-scale array.
 //  F32: row-major float[O][I].
 //
-// A row tile is therefore one contiguous byte range, which the GEMV streams
-// with one bulk copy per pipeline stage and which lands in shared memory in
-// exactly the order the lanes read it.
+// A row tile is therefore one contiguous byte range in which every lane's
+// 16 bytes of a block are its A fragment, loaded with one 16-byte load.
 //
 // Row permutations (the values are unchanged; only which logical row sits in
 // which tile row):

@@ -72,8 +72,6 @@ namespace {
 
 pc_status configure_device(pc_ctx *c) { return device_setup(c->dev, &c->nsm, &c->max_smem); }
 
-int nt_for_rows(int rows) { return rows <= 4 ? 1 : 2; }
-
 // CUDA events around one launch while profiling (pc_profile_begin/end).
 struct Prof {
     pc_ctx *c;
@@ -95,7 +93,7 @@ struct Prof {
 // Launch one GEMV over a device job list.
 pc_status run_gemv(pc_ctx *c, GemvParams p, int rows_per_job, const char *label) {
     p.err = c->err;
-    const int nt = nt_for_rows(p.shared_rows > 0 ? p.shared_rows : rows_per_job);
+    const int nt = gemv_nt_for_rows(p.shared_rows > 0 ? p.shared_rows : rows_per_job);
     if (!gemv_plan(p, nt, c->max_smem))
         return fail(PC_ERR_FORMAT, "GEMV input of " + std::to_string(p.Ip) + " columns does not fit in shared memory");
     Prof pr(c, label);
@@ -307,7 +305,9 @@ pc_status run_moe(pc_ctx *c, int l, const float *x, int M, const int *sel_in, co
     p.ldx = k.intermediate;
     p.y = c->eo;
     p.ldy = D;
-    p.shared_rows = shared_rows_for(M * K);  // B column = (token, k) pair
+    // B column = (token, k) pair when that keeps one N-tile; otherwise each
+    // expert's job fills B with just its own rows
+    p.shared_rows = gemv_nt_for_rows(M * K) == 1 ? M * K : 0;
     PC_TRY(run_gemv(c, p, rows, "expert_down"));
     if (ep) PC_TRY(ep_allreduce_sum(c, c->eo, (size_t)M * K * D));
     if (c->trace) {

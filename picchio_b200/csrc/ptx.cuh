@@ -120,35 +120,24 @@ __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
     return r;
 }
 
-// One 32-bit word of a T4 tile = one lane's A fragment of one m16n8k16 step:
-// nibbles (bits 0-3, 16-19) -> reg0, (4-7, 20-23) -> reg1, (8-11, 24-27) ->
-// reg2, (12-15, 28-31) -> reg3.  Each nibble n becomes the exact f16 value
-// n - 8: OR-ing n into the mantissa of 1024.0 gives 1024 + n (or 1024 + 16n
-// for the upper nibble of a byte), from which 1032 is subtracted (or which is
-// scaled by 1/16 and offset by -72); all steps are exact in f16.
-__device__ __forceinline__ void dequant_i4_word(uint32_t w, uint32_t (&a)[4]) {
-    const uint32_t MAGIC = 0x64006400u;
-    uint32_t t0 = lop3_and_or(w, 0x000F000Fu, MAGIC);
-    uint32_t t1 = lop3_and_or(w, 0x00F000F0u, MAGIC);
-    uint32_t w8 = w >> 8;
-    uint32_t t2 = lop3_and_or(w8, 0x000F000Fu, MAGIC);
-    uint32_t t3 = lop3_and_or(w8, 0x00F000F0u, MAGIC);
-    a[0] = hsub2_u32(t0, 0x64086408u);                 // - 1032
-    a[1] = hfma2_u32(t1, 0x2C002C00u, 0xD480D480u);    // * 1/16 - 72
-    a[2] = hsub2_u32(t2, 0x64086408u);
-    a[3] = hfma2_u32(t3, 0x2C002C00u, 0xD480D480u);
+// D = A(16x32 s8, row) * B(32x8 s8, col) + C, exact s32 accumulate.
+__device__ __forceinline__ void mma_s8_16832(int (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1,
+                                             const int (&c)[4]) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 "
+        "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%11,%12,%13};"
+        : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "r"(c[0]), "r"(c[1]), "r"(c[2]),
+          "r"(c[3]));
 }
 
-// Two 32-bit words of a T8 tile = one lane's A fragment of one step: bytes
-// (0,1) -> reg0, (2,3) -> reg1 of the first word, same for the second word
-// -> reg2, reg3.  Signed byte b becomes f16 (1024 + (b ^ 0x80)) - 1152 = b.
-__device__ __forceinline__ void dequant_i8_words(uint32_t w0, uint32_t w1, uint32_t (&a)[4]) {
-    const uint32_t MAGIC = 0x64646464u;
-    uint32_t u0 = w0 ^ 0x80808080u, u1 = w1 ^ 0x80808080u;
-    a[0] = hsub2_u32(prmt(u0, MAGIC, 0x4140u), 0x64806480u);
-    a[1] = hsub2_u32(prmt(u0, MAGIC, 0x4342u), 0x64806480u);
-    a[2] = hsub2_u32(prmt(u1, MAGIC, 0x4140u), 0x64806480u);
-    a[3] = hsub2_u32(prmt(u1, MAGIC, 0x4342u), 0x64806480u);
-}
+// One 32-bit word of a T4 tile holds 8 nibbles: the low nibble of each byte
+// belongs to one A register of an s8 MMA, the high nibble to another.  A
+// nibble n moved to the top of its byte and XOR-ed with 0x80 is the signed
+// byte 16 * (n - 8) exactly (n = 0 -> 0x80 = -128, n = 15 -> 0x70 = 112), so
+// each register costs one or two logic ops; the factor 16 is removed with the
+// row's exponent.
+__device__ __forceinline__ uint32_t nib_hi_s8(uint32_t w) { return (w & 0xF0F0F0F0u) ^ 0x80808080u; }
+__device__ __forceinline__ uint32_t nib_lo_s8(uint32_t w) { return ((w << 4) & 0xF0F0F0F0u) ^ 0x80808080u; }
 
 }  // namespace pc

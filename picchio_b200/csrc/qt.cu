@@ -148,7 +148,7 @@ pc_status pc_qt_matmul(pc_qt *w, const float *x_dev, float *y_dev, int S, void *
     p.y = y_dev;
     p.ldy = w->t.O;
     p.err = w->err;
-    const int nt = std::min(S, GEMV_MAXR) <= 4 ? 1 : 2;
+    const int nt = gemv_nt_for_rows(std::min(S, GEMV_MAXR));
     if (!gemv_plan(p, nt, w->max_smem)) return fail(PC_ERR_FORMAT, "input rows do not fit in shared memory");
     PC_CU(gemv_launch(p, nt, w->nsm, st));
     return PC_OK;

@@ -20,7 +20,9 @@ __device__ __forceinline__ int src_nibble(const uint8_t *q4, int O, int I, int r
 }
 
 // One thread per (row tile, block, lane): 16 bytes of nibbles (+ the scales
-// of rows g and g+8 for lanes with t == 0).
+// of rows g and g+8 for lanes with t == 0).  Word q = 2m + h of lane 4g + t
+// holds columns 64kc + 32m + 16h + 4t + j (j = 0..3) in byte j: row g in the
+// low nibble, row g + 8 in the high nibble.
 __global__ void retile_t4_kernel(const uint8_t *q4, const float *scales, int bs, TileDesc d) {
     const int64_t total = (int64_t)(d.Op / 16) * d.kblocks * 32;
     const int ng = bs > 0 ? (d.I + bs - 1) / bs : 1;
@@ -33,18 +35,13 @@ __global__ void retile_t4_kernel(const uint8_t *q4, const float *scales, int bs,
         const int rlo = tile_row_to_logical(d.perm, d.head_dim, rt, g);
         const int rhi = tile_row_to_logical(d.perm, d.head_dim, rt, g + 8);
         uint32_t w[4];
-        for (int s = 0; s < 4; ++s) {
-            const int c = kc * 64 + s * 16 + 2 * t;
+        for (int q = 0; q < 4; ++q) {
+            const int c = kc * 64 + 32 * (q >> 1) + 16 * (q & 1) + 4 * t;
             uint32_t v = 0;
-            v |= (uint32_t)src_nibble(q4, d.O, d.I, rlo, c) << 0;
-            v |= (uint32_t)src_nibble(q4, d.O, d.I, rlo, c + 1) << 16;
-            v |= (uint32_t)src_nibble(q4, d.O, d.I, rhi, c) << 4;
-            v |= (uint32_t)src_nibble(q4, d.O, d.I, rhi, c + 1) << 20;
-            v |= (uint32_t)src_nibble(q4, d.O, d.I, rlo, c + 8) << 8;
-            v |= (uint32_t)src_nibble(q4, d.O, d.I, rlo, c + 9) << 24;
-            v |= (uint32_t)src_nibble(q4, d.O, d.I, rhi, c + 8) << 12;
-            v |= (uint32_t)src_nibble(q4, d.O, d.I, rhi, c + 9) << 28;
-            w[s] = v;
+            for (int j = 0; j < 4; ++j)
+                v |= ((uint32_t)src_nibble(q4, d.O, d.I, rlo, c + j) << (8 * j)) |
+                     ((uint32_t)src_nibble(q4, d.O, d.I, rhi, c + j) << (8 * j + 4));
+            w[q] = v;
         }
         uint8_t *dst = d.tiles + blk * d.blk_bytes;
         *reinterpret_cast<uint4 *>(dst + L * 16) = make_uint4(w[0], w[1], w[2], w[3]);
@@ -66,6 +63,8 @@ __device__ __forceinline__ uint32_t src_byte(const int8_t *q8, int O, int I, int
     return (uint32_t)(uint8_t)q8[(int64_t)row * I + col];
 }
 
+// Word 2h + r of lane 4g + t holds columns 32kc + 16h + 4t + j in byte j, of
+// row g (r = 0) or g + 8 (r = 1): the lane's A fragment of one m16n8k32 step.
 __global__ void retile_t8_kernel(const int8_t *q8, TileDesc d) {
     const int64_t total = (int64_t)(d.Op / 16) * d.kblocks * 32;
     for (int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; idx < total;
@@ -74,16 +73,13 @@ __global__ void retile_t8_kernel(const int8_t *q8, TileDesc d) {
         const int64_t blk = idx >> 5;
         const int kc = (int)(blk % d.kblocks), rt = (int)(blk / d.kblocks);
         const int g = L >> 2, t = L & 3;
-        const int rlo = tile_row_to_logical(d.perm, d.head_dim, rt, g);
-        const int rhi = tile_row_to_logical(d.perm, d.head_dim, rt, g + 8);
+        const int rows[2] = {tile_row_to_logical(d.perm, d.head_dim, rt, g),
+                             tile_row_to_logical(d.perm, d.head_dim, rt, g + 8)};
         uint32_t w[4];
-        for (int s = 0; s < 2; ++s) {
-            const int c = kc * 32 + s * 16 + 2 * t;
-            w[2 * s] = src_byte(q8, d.O, d.I, rlo, c) | (src_byte(q8, d.O, d.I, rlo, c + 1) << 8) |
-                       (src_byte(q8, d.O, d.I, rhi, c) << 16) | (src_byte(q8, d.O, d.I, rhi, c + 1) << 24);
-            w[2 * s + 1] = src_byte(q8, d.O, d.I, rlo, c + 8) | (src_byte(q8, d.O, d.I, rlo, c + 9) << 8) |
-                           (src_byte(q8, d.O, d.I, rhi, c + 8) << 16) |
-                           (src_byte(q8, d.O, d.I, rhi, c + 9) << 24);
+        for (int q = 0; q < 4; ++q) {
+            const int c = kc * 32 + 16 * (q >> 1) + 4 * t, r = rows[q & 1];
+            w[q] = src_byte(q8, d.O, d.I, r, c) | (src_byte(q8, d.O, d.I, r, c + 1) << 8) |
+                   (src_byte(q8, d.O, d.I, r, c + 2) << 16) | (src_byte(q8, d.O, d.I, r, c + 3) << 24);
         }
         *reinterpret_cast<uint4 *>(d.tiles + blk * d.blk_bytes + L * 16) = make_uint4(w[0], w[1], w[2], w[3]);
     }
@@ -118,26 +114,25 @@ __global__ void dequant_tiles_kernel(TileDesc d, float *out) {
         int rt, tr;
         logical_to_tile(d.perm, d.head_dim, lr, rt, tr);
         const int g = tr & 7, rh = tr >> 3;
-        const int cc = c & 15, t = (cc & 7) >> 1, up8 = cc >> 3, odd = cc & 1;
-        const int L = 4 * g + t;
         float v, s;
         if (d.fmt == TF_T4) {
-            const int kc = c / 64, step = (c % 64) / 16;
+            const int kc = c / 64, r = c % 64;
+            const int q = 2 * (r / 32) + (r % 32) / 16, t = (r % 16) / 4, j = r % 4;
             const uint8_t *blk = d.tiles + ((int64_t)rt * d.kblocks + kc) * d.blk_bytes;
-            const uint32_t w = *reinterpret_cast<const uint32_t *>(blk + L * 16 + step * 4);
-            const int bit = 4 * rh + 8 * up8 + 16 * odd;
-            v = (float)((int)((w >> bit) & 0xF) - 8);
+            const uint32_t w = *reinterpret_cast<const uint32_t *>(blk + (4 * g + t) * 16 + q * 4);
+            v = (float)((int)((w >> (8 * j + 4 * rh)) & 0xF) - 8);
             if (d.gs > 0) {
-                const int gpc = 64 / d.gs, j = (c % 64) / d.gs;
-                s = reinterpret_cast<const float *>(blk + 512)[g * gpc * 2 + j * 2 + rh];
+                const int gpc = 64 / d.gs, jg = r / d.gs;
+                s = reinterpret_cast<const float *>(blk + 512)[g * gpc * 2 + jg * 2 + rh];
             } else {
                 s = d.rs[lr];
             }
         } else {
-            const int kc = c / 32, step = (c % 32) / 16;
+            const int kc = c / 32, r = c % 32;
+            const int q = 2 * (r / 16) + rh, t = (r % 16) / 4, j = r % 4;
             const uint8_t *blk = d.tiles + ((int64_t)rt * d.kblocks + kc) * d.blk_bytes;
-            const uint32_t w = *reinterpret_cast<const uint32_t *>(blk + L * 16 + (2 * step + up8) * 4);
-            v = (float)(int8_t)((w >> (8 * (2 * rh + odd))) & 0xFF);
+            const uint32_t w = *reinterpret_cast<const uint32_t *>(blk + (4 * g + t) * 16 + q * 4);
+            v = (float)(int8_t)((w >> (8 * j)) & 0xFF);
             s = d.rs[lr];
         }
         out[idx] = __fmul_rn(v, s);
