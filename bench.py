@@ -66,48 +66,64 @@ def traffic_from_profiles():
 
 
 class Clocks:
-    """nvidia-smi sampling during the timed region."""
+    """nvidia-smi sampling (every 100 ms) started before the warm-up; summary()
+    keeps the samples taken inside the timed window (host wall clock)."""
+
+    FIELDS = ("timestamp,clocks.sm,clocks.max.sm,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
 
     def __init__(self, dev):
         self.dev = dev
         self.p = None
-
-    def __enter__(self):
+        self.out = ""
+        self.t0 = self.t1 = None
         try:
-            self.p = subprocess.Popen(
-                ["nvidia-smi", "-i", str(self.dev), "--query-gpu=clocks.sm,clocks.max.sm,clocks_event_reasons.active,"
-                 "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-                 "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap",
-                 "--format=csv,noheader,nounits", "-lms", "200"],
-                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.p = subprocess.Popen(["nvidia-smi", "-i", str(dev), f"--query-gpu={self.FIELDS}",
+                                       "--format=csv,noheader,nounits", "-lms", "100"],
+                                      stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except Exception:
             self.p = None
+
+    def __enter__(self):
+        self.t0 = time.time()
         return self
 
     def __exit__(self, *a):
-        self.out = ""
+        self.t1 = time.time()
+
+    def stop(self):
         if self.p:
             self.p.terminate()
             try:
                 self.out, _ = self.p.communicate(timeout=5)
             except Exception:
                 self.p.kill()
+            self.p = None
 
     def summary(self):
-        rows = []
+        import datetime
+        self.stop()
+        rows, inside = [], []
         for line in (self.out or "").splitlines():
             f = [x.strip() for x in line.split(",")]
-            if len(f) >= 7:
-                try:
-                    rows.append((float(f[0]), float(f[1]), f[3:]))
-                except ValueError:
-                    pass
-        if not rows:
+            if len(f) < 8:
+                continue
+            try:
+                ts = datetime.datetime.strptime(f[0], "%Y/%m/%d %H:%M:%S.%f").timestamp()
+                r = (float(f[1]), float(f[2]), f[4:8])
+            except ValueError:
+                continue
+            rows.append(r)
+            if self.t0 is not None and self.t0 <= ts <= self.t1:
+                inside.append(r)
+        use = inside or rows
+        if not use:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for r in rows for i, v in enumerate(r[2]) if v.lower().startswith("active")})
-        return {"sm_mhz": statistics.median(r[0] for r in rows), "sm_max_mhz": max(r[1] for r in rows),
-                "reasons": reasons, "samples": len(rows)}
+        reasons = sorted({names[i] for r in use for i, v in enumerate(r[2]) if v.lower().startswith("active")})
+        return {"sm_mhz": statistics.median(r[0] for r in use), "sm_max_mhz": max(r[1] for r in use),
+                "reasons": reasons, "samples": len(use), "window": "timed" if inside else "whole run"}
 
 
 def dist_setup():
@@ -170,7 +186,7 @@ def run_reference(args, world, rank):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=64)
+    ap.add_argument("--steps", type=int, default=256)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--layers", type=int, default=36, help="fewer layers: quick checks only, not a bench value")
@@ -196,6 +212,9 @@ def main():
                         kv_bf16=False)
     t_init = time.time() - t0
     m.kv_fill_synthetic(CTX_PREFIX)
+    clk = Clocks(local)
+    import atexit
+    atexit.register(clk.stop)
     pos = CTX_PREFIX
     tok = 1
     # warm-up (graph capture + first replays)
@@ -205,7 +224,7 @@ def main():
     barrier(world)
     torch.cuda.synchronize()
     l0 = m.launches
-    with Clocks(local) as clk:
+    with clk:
         ids, dev_ms = m.generate_device(tok, pos, args.steps)
     torch.cuda.synchronize()
     barrier(world)
@@ -250,7 +269,8 @@ def main():
         "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": dev_ms / args.steps, "higher_is_better": True,
         "scaling": "strong" if world > 1 else "weak", "vs_baseline": None,
-        "dtype": "int4/int8 weights, f16 hi/lo tensor-core MMA with fp32 accumulate, fp32 activations",
+        "dtype": "int4/int8 weights; s8 tensor-core MMA on 3-digit int8 splits of the fp32 activations "
+                 "(exact s32 group sums), fp32 accumulate",
         "data": "synthetic (seeded random-init weights generated on device; synthetic 4096-position KV prefix)",
         "config": {"workload": "GPT-OSS-120B-shaped bs1 greedy decode at context 4096 (BASELINE configs[4])",
                    "model": "gpt-oss-120b-shape", "layers": cfg.n_layers, "experts": cfg.n_experts,
