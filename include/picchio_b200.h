@@ -159,9 +159,9 @@ pc_status pc_set_trace(pc_ctx *ctx, int on);
 pc_status pc_get_stage(pc_ctx *ctx, const char *name, float *out, int n);
 pc_status pc_dump(pc_ctx *ctx, const char *dir);  /* writes <name>.npy like ORACLE_DIR */
 
-/* Expert residency with streaming (opts.expert_residency == 1): copies the
- * listed experts of `layer` from pinned host memory into the layer's HBM cache
- * on the side stream, like prefetch_issue (picchio.c:1180-1230) but exact. */
+/* Expert prefetch hint, the counterpart of prefetch_issue
+ * (picchio.c:1180-1230).  Every expert is resident in HBM (the only residency
+ * mode built), so this validates its arguments and returns PC_OK. */
 pc_status pc_expert_prefetch(pc_ctx *ctx, int layer, const int *eids, int n);
 
 /* ---- weight-level operator: matmul_qt (quant.h:323-337) ---------------- */

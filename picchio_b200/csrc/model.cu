@@ -812,7 +812,8 @@ pc_status pc_dump(pc_ctx *c, const char *dir) {
 
 pc_status pc_expert_prefetch(pc_ctx *c, int layer, const int *eids, int n) {
     if (!c) return fail(PC_ERR_INVALID_ARG, "null context");
-    (void)layer; (void)eids; (void)n;
+    if (layer < 0 || layer >= c->cfg.n_layers || n < 0 || (n > 0 && !eids))
+        return fail(PC_ERR_INVALID_ARG, "bad pc_expert_prefetch arguments");
     // Every expert is resident in HBM in this build: nothing to fetch.
     return PC_OK;
 }
