@@ -175,6 +175,21 @@ pc_status pc_qt_create(int device, int fmt, int O, int I, int block_size, const 
                        const float *scales, pc_qt **out);
 /* y_dev[S][O] = x_dev[S][I] . W^T on `stream` (a cudaStream_t, NULL = default). */
 pc_status pc_qt_matmul(pc_qt *w, const float *x_dev, float *y_dev, int S, void *stream);
+/* The same product as pc_qt_matmul, bit for bit, for callers that must not
+ * allocate device memory during the call: code running under a memory budget
+ * that forbids new allocations, or that cannot afford the implicit
+ * synchronization cudaMalloc brings.  pc_qt_matmul allocates a job table the
+ * first time it sees each row count S; this entry point allocates nothing, at
+ * any call: its scratch (job table, job count, error word, ~1 KB) is a static
+ * device array of this library, set up once per device on the first call
+ * (cudaGetSymbolAddress plus a synchronous clear of the error word) - make
+ * that first call before any stream capture that would include it.
+ * Limits: S <= PC_QT_NOALLOC_MAX_ROWS (PC_ERR_RANGE beyond); one scratch per
+ * device, so calls that overlap in time (other streams or threads) race and
+ * must be serialized by the caller.  No counterpart in the reference, whose
+ * matmul_qt (quant.h:323-337) runs on the host with caller-owned buffers. */
+#define PC_QT_NOALLOC_MAX_ROWS 64
+pc_status pc_qt_matmul_noalloc(pc_qt *w, const float *x_dev, float *y_dev, int S, void *stream);
 /* out_dev[O][I] = dequantized weights, (nibble-8)*scale in fp32. */
 pc_status pc_qt_dequant(pc_qt *w, float *out_dev, void *stream);
 void pc_qt_free(pc_qt *w);

@@ -134,6 +134,7 @@ def lib():
         L.pc_expert_prefetch.argtypes = [vp, C.c_int, ip, C.c_int]
         L.pc_qt_create.argtypes = [C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, vp, fp, C.POINTER(vp)]
         L.pc_qt_matmul.argtypes = [vp, vp, vp, C.c_int, vp]
+        L.pc_qt_matmul_noalloc.argtypes = [vp, vp, vp, C.c_int, vp]
         L.pc_qt_dequant.argtypes = [vp, vp, vp]
         L.pc_qt_free.argtypes = [vp]
         L.pc_qt_free.restype = None
@@ -151,7 +152,7 @@ def lib():
             getattr(L, name).restype = st
         for name in ("pc_init", "pc_init_synthetic", "pc_get_config", "pc_forward_token", "pc_prefill",
                      "pc_decode_batch", "pc_get_logits", "pc_moe_layer", "pc_moe_experts", "pc_set_trace",
-                     "pc_get_stage", "pc_dump", "pc_expert_prefetch", "pc_qt_create", "pc_qt_matmul",
+                     "pc_get_stage", "pc_dump", "pc_expert_prefetch", "pc_qt_create", "pc_qt_matmul", "pc_qt_matmul_noalloc",
                      "pc_qt_dequant", "pc_nccl_unique_id", "pc_check_device"):
             getattr(L, name).restype = st
         _lib = L
@@ -337,6 +338,15 @@ class QT:
         y = torch.empty((x.shape[0], self.O), dtype=torch.float32, device=x.device)
         st = stream if stream is not None else torch.cuda.current_stream(x.device).cuda_stream
         _check(lib().pc_qt_matmul(self._h, _dev_ptr(x), _dev_ptr(y), x.shape[0], C.c_void_p(st)))
+        return y
+
+    def matmul_noalloc(self, x, out=None, stream=None):
+        """pc_qt_matmul_noalloc: the same product with no device allocation in
+        the library call (at most 64 rows); ``out`` may be given."""
+        import torch
+        y = out if out is not None else torch.empty((x.shape[0], self.O), dtype=torch.float32, device=x.device)
+        st = stream if stream is not None else torch.cuda.current_stream(x.device).cuda_stream
+        _check(lib().pc_qt_matmul_noalloc(self._h, _dev_ptr(x), _dev_ptr(y), x.shape[0], C.c_void_p(st)))
         return y
 
     def dequant(self):

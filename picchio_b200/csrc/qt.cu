@@ -6,12 +6,14 @@
 #include <algorithm>
 #include <cstring>
 #include <map>
+#include <mutex>
 #include <string>
 #include <vector>
 
 #include "context.h"
 #include "gemv.h"
 #include "kernels.h"
+#include "launch.cuh"
 
 struct pc_qt {
     int dev = 0, nsm = 148, max_smem = 0;
@@ -57,6 +59,68 @@ pc_status jobs_for(pc_qt *w, int S, std::pair<GemvJob *, int *> &out) {
     out = {dj, dc};
     w->jobs[S] = out;
     return PC_OK;
+}
+
+}  // namespace
+
+// ---- pc_qt_matmul_noalloc: the same product, for callers that cannot allocate
+//
+// Scratch lives in one file-scope device array per device: the GEMV job
+// table (up to PC_QT_NOALLOC_MAX_ROWS input rows = 8 jobs of 8 rows), its job
+// count and the kernel's error word.  Its address is taken once per device
+// with cudaGetSymbolAddress, when the error word (the only field that must
+// start at zero) is also cleared; every call rewrites the job table with a
+// one-warp kernel and then launches the GEMV on it.  Nothing is allocated,
+// so two calls that overlap (different streams or threads) race on it.
+
+namespace {
+
+constexpr int NOALLOC_MAX_JOBS = PC_QT_NOALLOC_MAX_ROWS / GEMV_MAXR;
+
+struct NoallocScratch {
+    GemvJob jobs[NOALLOC_MAX_JOBS];
+    int njobs;
+    int err;  // written by the GEMV on a fault; zero from set-up on
+};
+
+__device__ __align__(256) unsigned char g_noalloc_scratch[sizeof(NoallocScratch)];
+
+constexpr int NOALLOC_MAX_DEVICES = 64;
+std::mutex g_noalloc_mu;
+NoallocScratch *g_noalloc_ptr[NOALLOC_MAX_DEVICES] = {};
+
+// Once per device (the current one): the scratch address and a zeroed error word.
+pc_status noalloc_scratch(int dev, NoallocScratch **out) {
+    if (dev < 0 || dev >= NOALLOC_MAX_DEVICES) return fail(PC_ERR_INVALID_ARG, "device ordinal out of range");
+    std::lock_guard<std::mutex> lk(g_noalloc_mu);
+    if (!g_noalloc_ptr[dev]) {
+        void *p = nullptr;
+        cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(noalloc scratch)");
+        e = cudaMemset(p, 0, sizeof(NoallocScratch));
+        if (e != cudaSuccess) return cuda_fail(e, "clearing noalloc scratch");
+        g_noalloc_ptr[dev] = static_cast<NoallocScratch *>(p);
+    }
+    *out = g_noalloc_ptr[dev];
+    return PC_OK;
+}
+
+// One thread per job: the job table pc_qt_matmul builds on the host, rows
+// 8j..8j+7 of x into the same rows of y.
+__global__ void noalloc_jobs_kernel(NoallocScratch *s, const uint8_t *tiles, const float *rs, int n_rt, int O,
+                                    int S) {
+    const int nj = (S + GEMV_MAXR - 1) / GEMV_MAXR, j = threadIdx.x;
+    if (j == 0) s->njobs = nj;
+    if (j >= nj) return;
+    GemvJob g;
+    memset(&g, 0, sizeof g);
+    g.tiles = tiles;
+    g.rs = rs;
+    g.n_rt = n_rt;
+    g.O = O;
+    g.nrows = min(GEMV_MAXR, S - j * GEMV_MAXR);
+    for (int i = 0; i < g.nrows; ++i) g.in_row[i] = g.out_row[i] = j * GEMV_MAXR + i;
+    s->jobs[j] = g;
 }
 
 }  // namespace
@@ -148,6 +212,47 @@ pc_status pc_qt_matmul(pc_qt *w, const float *x_dev, float *y_dev, int S, void *
     p.y = y_dev;
     p.ldy = w->t.O;
     p.err = w->err;
+    const int nt = gemv_nt_for_rows(std::min(S, GEMV_MAXR));
+    if (!gemv_plan(p, nt, w->max_smem)) return fail(PC_ERR_FORMAT, "input rows do not fit in shared memory");
+    PC_CU(gemv_launch(p, nt, w->nsm, st));
+    return PC_OK;
+}
+
+pc_status pc_qt_matmul_noalloc(pc_qt *w, const float *x_dev, float *y_dev, int S, void *stream) {
+    if (!w || !x_dev || !y_dev || S < 1) return fail(PC_ERR_INVALID_ARG, "bad pc_qt_matmul_noalloc arguments");
+    if (S > PC_QT_NOALLOC_MAX_ROWS)
+        return fail(PC_ERR_RANGE, "pc_qt_matmul_noalloc takes at most " + std::to_string(PC_QT_NOALLOC_MAX_ROWS) +
+                                      " input rows");
+    PC_CU(cudaSetDevice(w->dev));
+    cudaStream_t st = (cudaStream_t)stream;
+    if (w->t.fmt == TF_F32) {  // the fp32 kernel uses no scratch
+        F32GemvParams f{};
+        f.W = w->t.f32; f.O = w->t.O; f.I = w->t.I; f.x = x_dev; f.ldx = w->t.I; f.M = S;
+        f.y = y_dev; f.ldy = w->t.O;
+        PC_CU(launch_gemv_f32(f, st));
+        return PC_OK;
+    }
+    NoallocScratch *s = nullptr;
+    PC_TRY(noalloc_scratch(w->dev, &s));
+    noalloc_jobs_kernel<<<1, 32, 0, st>>>(s, w->t.tiles, w->t.rs, w->t.Op / 16, w->t.O, S);
+    PC_CU(cudaGetLastError());
+    GemvParams p{};
+    p.jobs = s->jobs;
+    p.njobs = &s->njobs;
+    p.static_jobs = 0;  // the table is written by the kernel just launched
+    p.fmt = w->t.fmt;
+    p.gs = w->t.gs;
+    p.kblocks = w->t.kblocks;
+    p.blk_bytes = w->t.blk_bytes;
+    p.I = w->t.I;
+    p.Ip = w->t.Ip;
+    p.perm = PERM_NONE;
+    p.epi = EPI_STORE;
+    p.x = x_dev;
+    p.ldx = w->t.I;
+    p.y = y_dev;
+    p.ldy = w->t.O;
+    p.err = &s->err;
     const int nt = gemv_nt_for_rows(std::min(S, GEMV_MAXR));
     if (!gemv_plan(p, nt, w->max_smem)) return fail(PC_ERR_FORMAT, "input rows do not fit in shared memory");
     PC_CU(gemv_launch(p, nt, w->nsm, st));
