@@ -1,0 +1,242 @@
+// attention_core.cuh - decode attention over the KV cache with attention
+// sinks and the alternating sliding window: the score / softmax / P.V part of
+// gqa_attention (picchio.c:556-607) for one (row, KV head, span) work item.
+//
+// A work item takes one KV head of one row and a span of up to 256 positions
+// (split-K over positions), for all G <= 8 query heads that share the KV head
+// (GQA, picchio.c:568); 256 threads:
+//  scores: thread t owns one position; it loads the whole K row with 16-byte
+//    loads first, then forms each head's dot in the reference's sequential
+//    order (dot = dot + q[i]*k[i], i = 0..hd-1, unfused), times 1/sqrt(hd);
+//  softmax: per-head max and sum over the span (block reductions);
+//  P.V: thread (4 dims, position group) loads its V rows (16 bytes each) up
+//    front and accumulates p[g][t] * V[t][d..d+3] for all G heads; the 16
+//    position groups are then summed in a fixed order.
+// The last item of a (row, KV head) to finish (atomic ticket) merges the
+// spans with the sink, which joins the max and the denominator only
+// (picchio.c:586-596).
+#pragma once
+#include <cuda_bf16.h>
+
+#include "kernels.h"
+#include "ptx.cuh"
+
+namespace pc {
+
+namespace {
+
+
+constexpr int MAXG = 8, NT = ATTN_SPLIT, PG = 16;  // PG: position groups in P.V
+
+// 4 consecutive elements as floats
+__device__ __forceinline__ float4 load4(const float *p) { return *reinterpret_cast<const float4 *>(p); }
+__device__ __forceinline__ float4 load4(const __nv_bfloat16 *p) {
+    const uint2 a = *reinterpret_cast<const uint2 *>(p);
+    const float2 x = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&a.x));
+    const float2 y = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&a.y));
+    return make_float4(x.x, x.y, y.x, y.y);
+}
+
+// Shared memory of one work item.
+template <int HD>
+struct AttnSmem {
+    float qs[MAXG][HD];
+    float ps[MAXG][NT];
+    float wred[MAXG][NT / 32];
+    float mloc[MAXG], lloc[MAXG];
+    float ored[NT / 32][MAXG][HD];
+    float mrec[MAXG][64], lrec[MAXG][64];
+    bool last;
+};
+
+// One work item: span s of KV head kh of row m, run by NT threads (t =
+// threadIdx.x < NT) that synchronize on named barrier `bar`.
+template <typename T, int HD>
+__device__ __forceinline__ void attn_item(const AttnParams &a, int s, int kh, int m, AttnSmem<HD> &sm, int bar) {
+    auto &qs = sm.qs;
+    auto &ps = sm.ps;
+    auto &wred = sm.wred;
+    auto &mloc = sm.mloc;
+    auto &lloc = sm.lloc;
+    auto &ored = sm.ored;
+    auto &mrec = sm.mrec;
+    auto &lrec = sm.lrec;
+    bool &last = sm.last;
+    const T *Kc = reinterpret_cast<const T *>(a.kc);
+    const T *Vc = reinterpret_cast<const T *>(a.vc);
+    const int G = a.H / a.KVH, kvd = a.KVH * HD;
+    const int pos = a.row_pos[m];
+    int end = pos;
+    if (end >= a.ctx) end = a.ctx - 1;  // picchio.c:559-560
+    int start = 0;
+    if (a.window > 0) {
+        start = end - a.window + 1;
+        if (start < 0) start = 0;
+    }
+    const int p0 = start + s * NT;
+    const int cnt = max(0, min(NT, end + 1 - p0));
+    const int64_t cache0 = (int64_t)a.row_seq[m] * a.seq_stride + kh * HD;
+    const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
+    for (int i = t; i < G * HD; i += NT) qs[i / HD][i % HD] = a.q[(int64_t)m * a.H * HD + (kh * G) * HD + i];
+    named_bar_sync(bar, NT);
+    const float scale = __fdiv_rn(1.0f, sqrtf((float)HD));
+    if (t < cnt) {
+        const T *kr = Kc + cache0 + (int64_t)(p0 + t) * kvd;
+        float4 k4[HD / 4];
+#pragma unroll
+        for (int i = 0; i < HD / 4; ++i) k4[i] = load4(kr + 4 * i);
+        float dot[MAXG];
+#pragma unroll
+        for (int g = 0; g < MAXG; ++g) dot[g] = 0.0f;
+#pragma unroll
+        for (int i = 0; i < HD / 4; ++i) {
+            const float kv[4] = {k4[i].x, k4[i].y, k4[i].z, k4[i].w};
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+#pragma unroll
+                for (int g = 0; g < MAXG; ++g)
+                    if (g < G) dot[g] = __fadd_rn(dot[g], __fmul_rn(qs[g][4 * i + j], kv[j]));
+        }
+#pragma unroll
+        for (int g = 0; g < MAXG; ++g)
+            if (g < G) ps[g][t] = __fmul_rn(dot[g], scale);
+    }
+    named_bar_sync(bar, NT);
+    for (int g = 0; g < G; ++g) {
+        float v = t < cnt ? ps[g][t] : -INFINITY;
+        for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+        if (lane == 0) wred[g][warp] = v;
+    }
+    named_bar_sync(bar, NT);
+    if (t < G) {
+        float v = -INFINITY;
+        for (int w = 0; w < NT / 32; ++w) v = fmaxf(v, wred[t][w]);
+        mloc[t] = v;
+    }
+    named_bar_sync(bar, NT);
+    for (int g = 0; g < G; ++g) {
+        float e = 0.0f;
+        if (t < cnt) {
+            e = expf(__fsub_rn(ps[g][t], mloc[g]));
+            ps[g][t] = e;
+        }
+        for (int o = 16; o > 0; o >>= 1) e = __fadd_rn(e, __shfl_xor_sync(0xffffffffu, e, o));
+        if (lane == 0) wred[g][warp] = e;
+    }
+    named_bar_sync(bar, NT);
+    if (t < G) {
+        float v = 0.0f;
+        for (int w = 0; w < NT / 32; ++w) v = __fadd_rn(v, wred[t][w]);
+        lloc[t] = v;
+    }
+    // P.V: thread = (dq: 4 dims, pg: position group); positions pg, pg+16, ...
+    constexpr int DQ = HD / 4;            // dim quads per row
+    constexpr int TPG = NT / PG;          // threads per position group (16)
+    float4 acc[MAXG];
+#pragma unroll
+    for (int g = 0; g < MAXG; ++g) acc[g] = make_float4(0.f, 0.f, 0.f, 0.f);
+    {
+        const int dq0 = t % TPG, pg = t / TPG;
+        {  // HD <= 64: one quad of dims per thread; all lanes run the shuffles
+            const int dq = dq0;
+            const bool act = dq < DQ;
+            float4 vv[NT / PG];
+#pragma unroll
+            for (int k = 0; k < NT / PG; ++k) {
+                const int u = pg + PG * k;
+                vv[k] = (act && u < cnt) ? load4(Vc + cache0 + (int64_t)(p0 + u) * kvd + 4 * dq)
+                                         : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+            float4 ac[MAXG];
+#pragma unroll
+            for (int g = 0; g < MAXG; ++g) ac[g] = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+            for (int k = 0; k < NT / PG; ++k) {
+                const int u = pg + PG * k;
+                if (u >= cnt) break;
+#pragma unroll
+                for (int g = 0; g < MAXG; ++g)
+                    if (g < G) {
+                        const float pg_ = ps[g][u];
+                        ac[g].x = __fmaf_rn(pg_, vv[k].x, ac[g].x);
+                        ac[g].y = __fmaf_rn(pg_, vv[k].y, ac[g].y);
+                        ac[g].z = __fmaf_rn(pg_, vv[k].z, ac[g].z);
+                        ac[g].w = __fmaf_rn(pg_, vv[k].w, ac[g].w);
+                    }
+            }
+            // the two position groups of a warp (lanes l and l^16) first
+#pragma unroll
+            for (int g = 0; g < MAXG; ++g) {
+                ac[g].x = __fadd_rn(ac[g].x, __shfl_xor_sync(0xffffffffu, ac[g].x, 16));
+                ac[g].y = __fadd_rn(ac[g].y, __shfl_xor_sync(0xffffffffu, ac[g].y, 16));
+                ac[g].z = __fadd_rn(ac[g].z, __shfl_xor_sync(0xffffffffu, ac[g].z, 16));
+                ac[g].w = __fadd_rn(ac[g].w, __shfl_xor_sync(0xffffffffu, ac[g].w, 16));
+            }
+            if (lane < 16 && act)
+#pragma unroll
+                for (int g = 0; g < MAXG; ++g)
+                    if (g < G) *reinterpret_cast<float4 *>(&ored[warp][g][4 * dq]) = ac[g];
+        }
+    }
+    named_bar_sync(bar, NT);
+    const int stride = HD + 2;
+    for (int idx = t; idx < G * HD; idx += NT) {
+        const int g = idx / HD, d = idx % HD;
+        float o = 0.0f;
+#pragma unroll
+        for (int w = 0; w < NT / 32; ++w) o = __fadd_rn(o, ored[w][g][d]);
+        float *rec = a.part + (((int64_t)m * a.H + kh * G + g) * a.nsplit + s) * stride;
+        rec[2 + d] = o;
+        if (d == 0) {
+            rec[0] = cnt > 0 ? mloc[g] : -INFINITY;
+            rec[1] = cnt > 0 ? lloc[g] : 0.0f;
+        }
+    }
+    __threadfence();
+    named_bar_sync(bar, NT);
+    if (t == 0) {
+        unsigned *c = a.counter + m * a.KVH + kh;
+        last = atomicAdd(c, 1u) == (unsigned)(a.nsplit - 1);
+        if (last) *c = 0u;
+    }
+    named_bar_sync(bar, NT);
+    if (!last) return;
+    __threadfence();
+    // merge the spans: (m, l) of every span into shared memory first
+    for (int idx = t; idx < G * a.nsplit; idx += NT) {
+        const int g = idx / a.nsplit, k = idx % a.nsplit;
+        const float *rec = a.part + (((int64_t)m * a.H + kh * G + g) * a.nsplit + k) * stride;
+        if (k < 64) {
+            mrec[g][k] = __ldcg(rec);
+            lrec[g][k] = __ldcg(rec + 1);
+        }
+    }
+    named_bar_sync(bar, NT);
+    for (int idx = t; idx < G * HD; idx += NT) {
+        const int g = idx / HD, d = idx % HD, h = kh * G + g;
+        const float *rec0 = a.part + (((int64_t)m * a.H + h) * a.nsplit) * stride;
+        float M = a.sinks ? a.sinks[h] : -INFINITY;
+        for (int k = 0; k < a.nsplit; ++k) M = fmaxf(M, mrec[g][k]);
+        float L = a.sinks ? expf(__fsub_rn(a.sinks[h], M)) : 0.0f;
+        float O = 0.0f;
+        for (int k0 = 0; k0 < a.nsplit; k0 += 8) {
+            float ov[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) ov[j] = k0 + j < a.nsplit ? __ldcg(rec0 + (k0 + j) * stride + 2 + d) : 0.0f;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const int k = k0 + j;
+                if (k >= a.nsplit || lrec[g][k] == 0.0f) continue;
+                const float f = expf(__fsub_rn(mrec[g][k], M));
+                L = __fmaf_rn(lrec[g][k], f, L);
+                O = __fmaf_rn(ov[j], f, O);
+            }
+        }
+        a.out[(int64_t)m * a.H * HD + h * HD + d] = __fdiv_rn(O, L);
+    }
+}
+
+
+}  // namespace
+
+}  // namespace pc

@@ -105,6 +105,7 @@ struct GemvParams {
     float *y;               // output rows, stride ldy
     int ldy;
     int residual;           // EPI_STORE: accumulate into y
+    const float *res_src;   // EPI_STORE with residual: read the residual here (same indexing as y), or null = y
     float swiglu_limit, swiglu_alpha;
     // EPI_QKV
     const float *rope_cs, *rope_sn;  // [ctx][half]
