@@ -8,6 +8,7 @@
 #include <vector>
 
 #include "../../include/picchio_b200.h"
+#include "decode.h"
 #include "layout.h"
 
 namespace pc {
@@ -111,6 +112,12 @@ struct pc_ctx {
     int *h_err = nullptr;       // pinned mirror of the device error word
     std::vector<void *> allocs; // device allocations owned by the context
     void *pinned = nullptr;     // pinned staging block
+
+    // persistent decode kernel (decode.cu): 0 = not set up yet, 1 = used, -1 = not applicable
+    int dec_state = 0;
+    pc::DecodeArgs dec_args{};
+    size_t dec_smem = 0;
+    unsigned *gbar = nullptr;   // its grid barrier counter
 
     // on-device greedy loop (pc_generate)
     int *d_gen = nullptr;       // ids produced by the loop

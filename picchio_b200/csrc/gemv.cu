@@ -49,8 +49,8 @@ cudaError_t set_nt(int max_smem) {
 
 }  // namespace
 
-size_t gemv_smem_bytes(int nt, int Ip, int stages, int stage_bytes) {
-    return (size_t)off_end(nt, Ip) + (size_t)stages * stage_bytes;
+size_t gemv_smem_bytes(int fmt, int nt, int Ip, int blk_bytes) {
+    return (size_t)gemv_smem_need(fmt, nt, Ip, blk_bytes);
 }
 
 cudaError_t gemv_configure(int max_smem) {
@@ -60,18 +60,17 @@ cudaError_t gemv_configure(int max_smem) {
     return e;
 }
 
-// Launch plan: no staging buffers (the kernel sizes its L2 prefetch
-// distance itself).  False if the input rows' digits (nt * Ip * 8 bytes) do
-// not fit in shared memory.
+// Launch plan: false if the B operand (nt * Ip * 8 bytes) and the warps'
+// rings of weight steps do not fit in one CTA's shared memory.
 bool gemv_plan(GemvParams &p, int nt, int max_smem) {
-    if (off_end(nt, p.Ip) > max_smem) return false;
-    p.stages = 0;
-    p.stage_bytes = 0;
+    if (gemv_smem_bytes(p.fmt, nt, p.Ip, p.blk_bytes) > (size_t)max_smem) return false;
+    p.stages = gemv_ring_depth(p.fmt, nt);
+    p.stage_bytes = GEMV_CONSUMERS * gemv_step_blocks(p.fmt, nt) * p.blk_bytes;
     return true;
 }
 
 cudaError_t gemv_launch(const GemvParams &p, int nt, int grid, cudaStream_t st) {
-    const size_t smem = gemv_smem_bytes(nt, p.Ip, p.stages, p.stage_bytes);
+    const size_t smem = gemv_smem_bytes(p.fmt, nt, p.Ip, p.blk_bytes);
     switch (nt) {
         case 1: return go_nt<1>(p, grid, smem, st);
         case 2: return go_nt<2>(p, grid, smem, st);

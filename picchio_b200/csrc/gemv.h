@@ -7,13 +7,17 @@
 namespace pc {
 
 constexpr int GEMV_CONSUMERS = 12;
-// k-blocks a warp holds in registers per step (64-column T4 or 32-column T8 blocks)
-__host__ __device__ constexpr int gemv_step_blocks(int fmt) { return fmt == TF_T4 ? 4 : 8; }
+// k-blocks per step of a warp (64-column T4 or 32-column T8 blocks), and the
+// depth of its shared-memory ring of steps; both shrink with the N-tiles so
+// that the B operand and the rings fit in one CTA's shared memory.
+__host__ __device__ constexpr int gemv_step_blocks(int fmt, int nt) { return nt == 4 ? 2 : (fmt == TF_T4 ? 4 : 8); }
+__host__ __device__ constexpr int gemv_ring_depth(int fmt, int nt) { return nt == 1 ? (fmt == TF_T4 ? 4 : 3) : 2; }
 // N-tiles (8 MMA columns = 2 input rows x 4 digit columns) for a job of `rows` input rows
 inline int gemv_nt_for_rows(int rows) { return rows <= 2 ? 1 : rows <= 4 ? 2 : 4; }
 constexpr int GEMV_THREADS = 32 * GEMV_CONSUMERS;
 
-size_t gemv_smem_bytes(int nt, int Ip, int stages, int stage_bytes);
+// Dynamic shared memory of one GEMV launch.
+size_t gemv_smem_bytes(int fmt, int nt, int Ip, int blk_bytes);
 cudaError_t gemv_configure(int max_smem);
 bool gemv_plan(GemvParams &p, int nt, int max_smem);
 cudaError_t gemv_launch(const GemvParams &p, int nt, int grid, cudaStream_t st);

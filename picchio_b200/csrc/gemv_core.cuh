@@ -60,7 +60,11 @@ struct SMeta {
 static_assert(sizeof(SMeta) <= 640, "meta region");
 
 __host__ __device__ inline int off_B(int nt) { return (OFF_RED + NRED * nt * NCONS * 256 + 127) & ~127; }
-__host__ __device__ inline int off_end(int nt, int Ip) { return (off_B(nt) + nt * Ip * 8 + 127) & ~127; }
+__host__ __device__ inline int off_ring(int nt, int Ip) { return (off_B(nt) + nt * Ip * 8 + 127) & ~127; }
+// Shared memory of one CTA: fixed regions, the B operand, the warps' rings.
+__host__ __device__ inline int gemv_smem_need(int fmt, int nt, int Ip, int blk_bytes) {
+    return off_ring(nt, Ip) + NCONS * gemv_ring_depth(fmt, nt) * gemv_step_blocks(fmt, nt) * blk_bytes;
+}
 
 // Signed digits of v (|v| <= 2^22): v = hi * 2^16 + mid * 2^8 + lo with
 // lo, mid in [-128, 127] and |hi| <= 64.
@@ -275,6 +279,23 @@ __device__ __forceinline__ void scale4(float (&acc)[4], const int (&d)[4], uint3
     acc[3] = __fmaf_rn(__int2float_rn(d[3]), b, acc[3]);
 }
 
+// The same from a block staged in shared memory.
+template <int FMT, int GS>
+__device__ __forceinline__ void load_blk_smem(BlkRegs &r, const uint8_t *blk, int lane) {
+    const int g = lane >> 2;
+    r.a = *reinterpret_cast<const uint4 *>(blk + lane * 16);
+    if (FMT == TF_T4 && GS == 32) {
+        r.s = *reinterpret_cast<const uint4 *>(blk + 512 + g * 16);
+    } else if (FMT == TF_T4 && GS == 64) {
+        const uint2 v = *reinterpret_cast<const uint2 *>(blk + 512 + g * 8);
+        r.s.x = v.x;
+        r.s.y = v.y;
+    } else if (FMT == TF_T4 && GS == 16) {
+        r.s = *reinterpret_cast<const uint4 *>(blk + 512 + g * 32);
+        r.s2 = *reinterpret_cast<const uint4 *>(blk + 512 + g * 32 + 16);
+    }
+}
+
 // One T4 block (64 columns = two s8 MMA steps) of one lane.  Grouped scales:
 // each group's sum is exact in s32 and is scaled into the fp32 accumulator
 // acc, the structure of matmul_i4_gs (quant.h:259-319); per-row scale (GS 0):
@@ -487,11 +508,13 @@ constexpr int BAR_FILL = 1;  // named barrier 1: all threads (B refills); 2..15:
 // INT4 group size (0 = per row).
 // The GEMV work of one CTA (index cta of ncta) over the job list of p.  PDL:
 // the launch is a programmatic dependent launch (gemv_kernel); the persistent
-// decode kernel calls this with PDL = false between its own grid barriers.
-template <int FMT, int NT, int GS, bool PDL>
+// decode kernel calls this with PDL = false between its own grid barriers,
+// and with smaller register steps (MBX blocks) to leave it registers.
+template <int FMT, int NT, int GS, bool PDL, int MBX = 0>
 __device__ __forceinline__ void gemv_cta(const GemvParams &p, uint8_t *smem, int cta, int ncta) {
     constexpr int CPB = FMT == TF_T4 ? 2 : 1;  // 32-column MMA steps per block
-    constexpr int MB = gemv_step_blocks(FMT);
+    constexpr int MB = MBX > 0 ? MBX : gemv_step_blocks(FMT, NT);  // blocks per step
+    constexpr int R = gemv_ring_depth(FMT, NT);  // steps per warp ring (R - 1 in flight)
     int *jp = reinterpret_cast<int *>(smem + OFF_JP);
     const uint8_t **stiles = reinterpret_cast<const uint8_t **>(smem + OFF_TILES);
     GemvJob *sjobs = reinterpret_cast<GemvJob *>(smem + OFF_JOBS);
@@ -606,25 +629,38 @@ __device__ __forceinline__ void gemv_cta(const GemvParams &p, uint8_t *smem, int
             advance(pf_u, pf_j);
         }
     };
-    int ld_u, ld_j, ld_c = 0;
+    // This warp's ring of R step slots in shared memory, filled with
+    // cp.async (16 bytes per lane per copy, no registers held while in flight):
+    // step s lives in slot s % R; R - 1 steps are in flight behind the one
+    // being computed.
+    uint8_t *myring = smem + off_ring(NT, p.Ip) + (size_t)cw * R * MB * BB;
+    const int sbytes = BB - 512;  // group-scale bytes per block (T4 with groups)
+    int ld_u, ld_j, ld_c = 0, ld_seq = 0;
     first_from(j0, ld_u, ld_j);
-    auto load_step = [&](BlkRegs(&f)[MB]) {  // loads step (ld_u, ld_c), then moves the cursor on
+    auto issue_step = [&]() {  // copies step (ld_u, ld_c), then moves the cursor on
         if (ld_u < u1) {
             const int nb = step_blocks(ld_c);
             const uint8_t *src = slice(ld_u, ld_j) + (size_t)ld_c * MB * BB;
+            uint8_t *dst = myring + (size_t)(ld_seq % R) * MB * BB;
 #pragma unroll
-            for (int i = 0; i < MB; ++i)
-                if (i < nb) load_blk<FMT, GS>(f[i], src + i * BB, lane);
+            for (int i = 0; i < MB; ++i) {
+                if (i < nb) {
+                    cp_async16(dst + i * BB + lane * 16, src + (size_t)i * BB + lane * 16);
+                    if (lane * 16 < sbytes)
+                        cp_async16(dst + i * BB + 512 + lane * 16, src + (size_t)i * BB + 512 + lane * 16);
+                }
+            }
             if (++ld_c == nch) {
                 ld_c = 0;
                 advance(ld_u, ld_j);
             }
         }
+        cp_async_commit();
+        ++ld_seq;
     };
     // weights do not depend on earlier kernels: start streaming before waiting for them
     for (int i = 0; i < PD; ++i) prefetch_next();
-    BlkRegs bufA[MB], bufB[MB];
-    load_step(bufA);
+    for (int i = 0; i < R - 1; ++i) issue_step();
 
     // inputs and outputs do
     if (PDL) pdl_wait();
@@ -651,10 +687,14 @@ __device__ __forceinline__ void gemv_cta(const GemvParams &p, uint8_t *smem, int
     float acc[NT][4];
     int ia[NT][4];
     const float W0 = (lane & 1) ? 1.0f : 65536.0f, W1 = (lane & 1) ? 0.0f : 256.0f;  // digit weights of my columns
-    // one step: load the next step into nxt, compute cur at chunk c (static
-    // buffer roles, so the two buffers alternate without register moves)
-    auto do_step = [&](BlkRegs(&cur)[MB], BlkRegs(&nxt)[MB], int c) {
-        load_step(nxt);
+    // one step: issue the step R - 1 ahead, wait for this one, compute it
+    int seq = 0;
+    auto do_step = [&](int c) {
+        issue_step();
+        cp_async_wait<R - 1>();
+        __syncwarp();  // every lane's copies of this step have landed
+        const uint8_t *slot = myring + (size_t)(seq % R) * MB * BB;
+        ++seq;
         const int nb = step_blocks(c);
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt)
@@ -664,19 +704,22 @@ __device__ __forceinline__ void gemv_cta(const GemvParams &p, uint8_t *smem, int
         for (int i = 0; i < MB; ++i) {
             if (i >= nb) break;
             const int kc = kb0 + c * MB + i;
+            BlkRegs r;
+            load_blk_smem<FMT, GS>(r, slot + i * BB, lane);
             if (FMT == TF_T4) {
                 uint4 B[NT];
 #pragma unroll
                 for (int nt = 0; nt < NT; ++nt)
                     B[nt] = reinterpret_cast<const uint4 *>(Bsm)[(nt * p.kblocks + kc) * 32 + lane];
-                block_t4<NT, GS>(cur[i], B, acc, ia);
+                block_t4<NT, GS>(r, B, acc, ia);
             } else {
                 uint2 B[NT];
 #pragma unroll
                 for (int nt = 0; nt < NT; ++nt) B[nt] = Bsm[(nt * p.kblocks + kc) * 32 + lane];
-                block_t8<NT>(cur[i], B, ia);
+                block_t8<NT>(r, B, ia);
             }
         }
+        __syncwarp();  // every lane is done with the slot before it is refilled
         if (FMT == TF_T8 || GS == 0) {  // per-row scale: the step's exact sums join the fp32 accumulator
 #pragma unroll
             for (int nt = 0; nt < NT; ++nt)
@@ -684,7 +727,6 @@ __device__ __forceinline__ void gemv_cta(const GemvParams &p, uint8_t *smem, int
                 for (int i = 0; i < 4; ++i) acc[nt][i] = __fadd_rn(acc[nt][i], __int2float_rn(ia[nt][i]));
         }
     };
-    bool odd = false;  // which buffer holds the current step
     int n = 0;         // this group's units done
     const int gbar = 2 + 2 * gi * NS;  // named barriers of this group: full/free per slot
     for (int j = j0; j < nj; ++j) {  // every warp visits every job segment, in order
@@ -716,11 +758,7 @@ __device__ __forceinline__ void gemv_cta(const GemvParams &p, uint8_t *smem, int
             for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
                 for (int i = 0; i < 4; ++i) acc[nt][i] = 0.f;
-            for (int c = 0; c < nch; ++c) {
-                if (odd) do_step(bufB, bufA, c);
-                else do_step(bufA, bufB, c);
-                odd = !odd;
-            }
+            for (int c = 0; c < nch; ++c) do_step(c);
             // digits -> value: lanes 4g + 2m hold (hi, mid), lanes 4g + 2m + 1 (lo, 0) of input row 2nt + m
             float v[NT][2];
 #pragma unroll

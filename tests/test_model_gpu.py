@@ -180,3 +180,22 @@ def test_bf16_kv_cache_stays_close(variant):
         a.prefill_tokens(m["prompt"], 0)
         b.prefill_tokens(m["prompt"], 0)
         assert rel_l2(b.logits(0), a.logits(0)) < 1e-2
+
+
+def test_persistent_decode_kernel_matches_reference(monkeypatch):
+    """The persistent batch-1 decode kernel (opt-in, PICCHIO_PERSISTENT=1)
+    gives the reference's greedy ids, per token (pc_forward_token) and in one
+    multi-token launch (pc_generate)."""
+    from picchio_b200 import Model
+    m = meta("tiny_gs32_i8")
+    import tempfile
+    d = tempfile.mkdtemp()
+    make_model(d, SynthConfig(**m["options"]), m["seed"])
+    monkeypatch.setenv("PICCHIO_PERSISTENT", "1")
+    with Model(d, ctx=m["ctx"]) as model:
+        ids = model.generate(m["prompt"], m["steps"])
+        assert ids == m["ids_batched"]
+        n = len(m["prompt"])
+        tok = model.prefill_tokens(m["prompt"], 0)
+        dev, _ = model.generate_device(tok, n, 32)
+        assert [tok] + dev[:31] == m["ids_batched"][:32]
