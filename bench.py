@@ -183,6 +183,83 @@ def run_reference(args, world, rank):
     print(json.dumps(line), flush=True)
 
 
+BS64 = 64
+
+
+def bs64_decode(m, ctx0, pos0, steps=16, warmup=3):
+    """Batch-64 greedy decode (BASELINE metric's bs64 leg): 64 sequences, each
+    with a seeded 4096-position KV prefix, one pc_decode_batch call per step
+    (host ints in and out), host clock over the timed steps."""
+    for s in range(1, BS64):
+        m.kv_fill_synthetic(ctx0, seq=s, seed=99 + s)
+    toks = [(7 * s + 1) % 1000 for s in range(BS64)]
+    pos = [pos0] * BS64
+    for _ in range(warmup):
+        toks = m.decode_batch(toks, pos)
+        pos = [p + 1 for p in pos]
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        toks = m.decode_batch(toks, pos)
+        pos = [p + 1 for p in pos]
+    dt = time.perf_counter() - t0
+    # per-kernel device time of one more step (CUDA events around every launch)
+    m.profile_begin()
+    toks = m.decode_batch(toks, pos)
+    prof = m.profile_end()
+    return {"value": BS64 * steps / dt, "unit": "tok/s", "batch": BS64, "steps": steps, "warmup": warmup,
+            "context": ctx0, "kv": "fp32", "ms_per_step": dt * 1e3 / steps,
+            "timing": "host clock around pc_decode_batch (H2D of 64 tokens + positions, D2H of 64 ids per step)",
+            "kernel_ms_per_step": {k: v[0] for k, v in prof.items()}}
+
+
+def moe_micro(dev, iters=20):
+    """one GPT-OSS-shaped expert layer (d_model 2880, FFN
+    2880, 32 experts, INT4 gs32), M tokens routed to 4 experts each with
+    uniform-random top-4 indices; expert GEMV bytes (distinct experts x
+    (gate_up + down tiles + biases)) over the CUDA-event time of the expert
+    half of moe_forward (pc_moe_experts, which synchronizes on every call:
+    "us" / "expert_gbs"), and over the device time of the two expert GEMV
+    kernels alone (events around each launch: "gemv_us" / "gemv_gbs")."""
+    import numpy as np
+    import torch
+    from picchio_b200 import Model, ModelConfig
+    cfg = ModelConfig(hidden=2880, n_layers=1, n_heads=64, n_kv_heads=8, head_dim=64, n_experts=32, topk=4,
+                      intermediate=2880, vocab=1024)
+    mm = Model.synthetic(cfg, seed=5, ctx=64, device=dev, max_batch=512)
+    gs = cfg.group_size
+    per_expert = ((2 * cfg.intermediate) // 16) * (cfg.hidden // 64) * (512 + (64 // gs) * 64) + 8 * cfg.intermediate \
+        + (cfg.hidden // 16) * (cfg.intermediate // 64) * (512 + (64 // gs) * 64) + 4 * cfg.hidden
+    rng = np.random.default_rng(11)
+    out = []
+    for M in (1, 4, 64, 512):
+        sel = np.stack([rng.choice(32, 4, replace=False) for _ in range(M)]).astype(np.int32)
+        w = rng.random((M, 4)).astype(np.float32)
+        w /= w.sum(1, keepdims=True)
+        x = torch.from_numpy(rng.standard_normal((M, cfg.hidden)).astype(np.float32)).cuda(dev)
+        s_d, w_d = torch.from_numpy(sel).cuda(dev), torch.from_numpy(w).cuda(dev)
+        for _ in range(3):
+            mm.moe_experts(x, s_d, w_d, 0)
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(iters):
+            mm.moe_experts(x, s_d, w_d, 0)
+        b.record()
+        torch.cuda.synchronize()
+        us = a.elapsed_time(b) * 1e3 / iters
+        mm.profile_begin()
+        for _ in range(iters):
+            mm.moe_experts(x, s_d, w_d, 0)
+        prof = mm.profile_end()
+        k_us = sum(prof.get(k, (0.0, 0))[0] for k in ("expert_gate_up", "expert_down")) * 1e3 / iters
+        distinct = len(set(sel.reshape(-1).tolist()))
+        out.append({"M": M, "us": us, "distinct_experts": distinct,
+                    "expert_gbs": distinct * per_expert / us / 1e3,
+                    "gemv_us": k_us, "gemv_gbs": distinct * per_expert / k_us / 1e3 if k_us else None})
+    mm.close()
+    return out
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -191,6 +268,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--layers", type=int, default=36, help="fewer layers: quick checks only, not a bench value")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-extra", action="store_true", help="skip the bs64 and expert-microbench side measurements")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     world, rank, local = dist_setup()
@@ -206,10 +284,11 @@ def main():
     nid = bcast_bytes(nccl_unique_id() if (world > 1 and rank == 0) else None, world) if world > 1 else None
     cfg = ModelConfig.gpt_oss_120b()
     cfg.n_layers = args.layers
-    ctx = CTX_PREFIX + args.warmup + 2 * args.steps + 16
+    ctx = CTX_PREFIX + args.warmup + 2 * args.steps + 64
     t0 = time.time()
+    extra = world == 1 and not args.no_extra
     m = Model.synthetic(cfg, seed=2024, ctx=ctx, device=local, ep_rank=rank, ep_size=world, nccl_id=nid,
-                        kv_bf16=False)
+                        kv_bf16=False, max_batch=BS64 if extra else 1)
     t_init = time.time() - t0
     m.kv_fill_synthetic(CTX_PREFIX)
     clk = Clocks(local)
@@ -289,6 +368,10 @@ def main():
         "kernel_ms": {k: v[0] / v[1] for k, v in prof.items()},
         "clocks": clk.summary(),
     }
+    if extra:
+        line["bs64"] = bs64_decode(m, CTX_PREFIX, pos)
+        m.close()
+        line["moe_micro"] = moe_micro(local)
     if rank == 0 and world == 1 and not args.no_cpu:
         from oracle import cpu_baseline
         r = cpu_baseline.measure(ctx=CTX_PREFIX)

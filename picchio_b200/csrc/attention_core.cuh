@@ -77,14 +77,21 @@ __device__ __forceinline__ void attn_item(const AttnParams &a, int s, int kh, in
     const int cnt = max(0, min(NT, end + 1 - p0));
     const int64_t cache0 = (int64_t)a.row_seq[m] * a.seq_stride + kh * HD;
     const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
+    // The KV rows of the span do not depend on q: this thread's K row goes
+    // into registers and its V row into L2 before q is even loaded, so the
+    // cache's HBM latency is paid once, overlapped with q and the scores.
+    float4 k4[HD / 4];
+    if (t < cnt) {
+        const T *kr = Kc + cache0 + (int64_t)(p0 + t) * kvd;
+#pragma unroll
+        for (int i = 0; i < HD / 4; ++i) k4[i] = load4(kr + 4 * i);
+        const char *vr = reinterpret_cast<const char *>(Vc + cache0 + (int64_t)(p0 + t) * kvd);
+        for (int o = 0; o < (int)(HD * sizeof(T)); o += 128) prefetch_l2(vr + o);
+    }
     for (int i = t; i < G * HD; i += NT) qs[i / HD][i % HD] = a.q[(int64_t)m * a.H * HD + (kh * G) * HD + i];
     named_bar_sync(bar, NT);
     const float scale = __fdiv_rn(1.0f, sqrtf((float)HD));
     if (t < cnt) {
-        const T *kr = Kc + cache0 + (int64_t)(p0 + t) * kvd;
-        float4 k4[HD / 4];
-#pragma unroll
-        for (int i = 0; i < HD / 4; ++i) k4[i] = load4(kr + 4 * i);
         float dot[MAXG];
 #pragma unroll
         for (int g = 0; g < MAXG; ++g) dot[g] = 0.0f;

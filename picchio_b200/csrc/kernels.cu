@@ -65,12 +65,30 @@ __global__ void embed_kernel(int fmt, const void *table, const float *scales, in
 // one round trip in, one out.
 constexpr int NORM_THREADS = 256, NORM_V4 = 4;  // up to 4 float4 per thread (D <= 4096)
 
+// 1/sqrt(mean + eps) of a row from each thread's partial sum of squares.
+// The sum is taken in double, as quant.h:396-402 accumulates it; the
+// per-thread element order is the same wherever this is used, so fused and
+// unfused norms of one row agree bit for bit.
+__device__ float norm_scale(double s, int D, float eps) {
+    __shared__ double red[NORM_THREADS / 32];
+    __shared__ float rs;
+    const int tid = threadIdx.x;
+    for (int q = 16; q > 0; q >>= 1) s += __shfl_xor_sync(0xffffffffu, s, q);
+    if ((tid & 31) == 0) red[tid >> 5] = s;
+    __syncthreads();
+    if (tid < 32) {
+        double v = tid < NORM_THREADS / 32 ? red[tid] : 0.0;
+        for (int q = 16; q > 0; q >>= 1) v += __shfl_xor_sync(0xffffffffu, v, q);
+        if (tid == 0) rs = __fdiv_rn(1.0f, sqrtf(__fadd_rn((float)(v / D), eps)));
+    }
+    __syncthreads();
+    return rs;
+}
+
 __global__ void __launch_bounds__(NORM_THREADS) rmsnorm_kernel(const float *x, const float *w, float *out, int D,
                                                                 float eps) {
     pdl_wait();
     pdl_trigger();
-    __shared__ double red[NORM_THREADS / 32];
-    __shared__ float rs;
     const int m = blockIdx.x, tid = threadIdx.x;
     const float *xr = x + (int64_t)m * D;
     float *o = out + (int64_t)m * D;
@@ -92,17 +110,7 @@ __global__ void __launch_bounds__(NORM_THREADS) rmsnorm_kernel(const float *x, c
     } else {
         for (int i = tid; i < D; i += NORM_THREADS) s += (double)xr[i] * (double)xr[i];
     }
-    // sum of squares in double, as quant.h:396-402 accumulates it
-    for (int q = 16; q > 0; q >>= 1) s += __shfl_xor_sync(0xffffffffu, s, q);
-    if ((tid & 31) == 0) red[tid >> 5] = s;
-    __syncthreads();
-    if (tid < 32) {
-        double v = tid < NORM_THREADS / 32 ? red[tid] : 0.0;
-        for (int q = 16; q > 0; q >>= 1) v += __shfl_xor_sync(0xffffffffu, v, q);
-        if (tid == 0) rs = __fdiv_rn(1.0f, sqrtf(__fadd_rn((float)(v / D), eps)));
-    }
-    __syncthreads();
-    const float r = rs;
+    const float r = norm_scale(s, D, eps);
     if (vec) {
         const int n4 = D >> 2;
 #pragma unroll
@@ -312,11 +320,16 @@ __global__ void __launch_bounds__(256) router_kernel(const RouterParams r) {
 // One block per row; expert rows are taken four at a time with all their
 // loads in flight.  The fma chain runs in k order, as picchio.c:1445-1454
 // accumulates it; a failed expert (sel < 0) is skipped (picchio.c:1394).
+// With ln_w set (and h), the updated residual row is also normalised into
+// hn: the next layer's input RMSNorm (picchio.c:1680) or the final norm
+// (picchio.c:1712), computed exactly as rmsnorm_kernel computes it.
 __global__ void __launch_bounds__(NORM_THREADS) combine_kernel(const float *eo, const float *w, const int *sel,
-                                                                float scale, int K, int D, float *out, float *h) {
+                                                                float scale, int K, int D, float *out, float *h,
+                                                                const float *ln_w, float eps, float *hn) {
     pdl_wait();
     pdl_trigger();
     const int m = blockIdx.x, tid = threadIdx.x;
+    const bool norm = ln_w && h;
     float wk[16];
     bool ok[16];
 #pragma unroll
@@ -360,25 +373,52 @@ __global__ void __launch_bounds__(NORM_THREADS) combine_kernel(const float *eo, 
                 }
             }
         }
+        float4 wv[3];
 #pragma unroll
         for (int j = 0; j < 3; ++j) {
             const int i = tid + j * NORM_THREADS;
+            wv[j] = (norm && i < n4) ? reinterpret_cast<const float4 *>(ln_w)[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+        double s = 0.0;
+#pragma unroll
+        for (int j = 0; j < 3; ++j) {
+            const int i = tid + j * NORM_THREADS;
+            hv[j] = make_float4(__fadd_rn(hv[j].x, acc[j].x), __fadd_rn(hv[j].y, acc[j].y),
+                                __fadd_rn(hv[j].z, acc[j].z), __fadd_rn(hv[j].w, acc[j].w));
             if (i >= n4) continue;
             if (out) reinterpret_cast<float4 *>(out + (int64_t)m * D)[i] = acc[j];
-            if (h)
-                reinterpret_cast<float4 *>(h + (int64_t)m * D)[i] =
-                    make_float4(__fadd_rn(hv[j].x, acc[j].x), __fadd_rn(hv[j].y, acc[j].y),
-                                __fadd_rn(hv[j].z, acc[j].z), __fadd_rn(hv[j].w, acc[j].w));
+            if (h) reinterpret_cast<float4 *>(h + (int64_t)m * D)[i] = hv[j];
+            s += (double)hv[j].x * hv[j].x + (double)hv[j].y * hv[j].y + (double)hv[j].z * hv[j].z +
+                 (double)hv[j].w * hv[j].w;
+        }
+        if (!norm) return;
+        const float r = norm_scale(s, D, eps);
+#pragma unroll
+        for (int j = 0; j < 3; ++j) {
+            const int i = tid + j * NORM_THREADS;
+            if (i < n4)
+                reinterpret_cast<float4 *>(hn + (int64_t)m * D)[i] =
+                    make_float4(__fmul_rn(__fmul_rn(hv[j].x, r), wv[j].x), __fmul_rn(__fmul_rn(hv[j].y, r), wv[j].y),
+                                __fmul_rn(__fmul_rn(hv[j].z, r), wv[j].z), __fmul_rn(__fmul_rn(hv[j].w, r), wv[j].w));
         }
         return;
     }
+    float *hr = h ? h + (int64_t)m * D : nullptr;
+    double s = 0.0;
     for (int i = tid; i < D; i += NORM_THREADS) {
         float acc = 0.0f;
         for (int k = 0; k < K; ++k)
             if (ok[k < 16 ? k : 15]) acc = __fmaf_rn(wk[k < 16 ? k : 15], eo[((int64_t)m * K + k) * D + i], acc);
         if (out) out[(int64_t)m * D + i] = acc;
-        if (h) h[(int64_t)m * D + i] = __fadd_rn(h[(int64_t)m * D + i], acc);
+        if (hr) {
+            const float v = __fadd_rn(hr[i], acc);
+            hr[i] = v;
+            s += (double)v * (double)v;
+        }
     }
+    if (!norm) return;
+    const float r = norm_scale(s, D, eps);
+    for (int i = tid; i < D; i += NORM_THREADS) hn[(int64_t)m * D + i] = __fmul_rn(__fmul_rn(hr[i], r), ln_w[i]);
 }
 
 // ------------------------------------------------------------- f32 gemv ----
@@ -497,9 +537,11 @@ cudaError_t launch_router(const RouterParams &r, cudaStream_t st) {
 }
 
 cudaError_t launch_combine(const float *eo, const float *w, const int *sel, float scale, int M, int K,
-                           int D, float *out, float *h, cudaStream_t st) {
-    return launch_k(combine_kernel, dim3(M), dim3(NORM_THREADS), 0, st, eo, w, sel, scale, K, D, out, h);
-    return cudaGetLastError();
+                           int D, float *out, float *h, cudaStream_t st, const float *ln_w, float eps,
+                           float *hn) {
+    if (ln_w && (!h || !hn)) return cudaErrorInvalidValue;
+    return launch_k(combine_kernel, dim3(M), dim3(NORM_THREADS), 0, st, eo, w, sel, scale, K, D, out, h, ln_w,
+                    eps, hn);
 }
 
 cudaError_t launch_gemv_f32(const F32GemvParams &p, cudaStream_t st) {

@@ -67,9 +67,12 @@ struct RouterParams {
 cudaError_t launch_router(const RouterParams &r, cudaStream_t st);
 
 // out[m][i] = sum over k (in k order) of w[m][k]*scale * eo[m*K+k][i]
-// (picchio.c:1445-1454); h[m][i] += out[m][i] when h != null.
+// (picchio.c:1445-1454); h[m][i] += out[m][i] when h != null.  With ln_w
+// (h required) hn[m] = rmsnorm(h[m] after the add, ln_w, eps), bit-equal to
+// launch_rmsnorm on that row.
 cudaError_t launch_combine(const float *eo, const float *w, const int *sel, float scale, int M, int K,
-                           int D, float *out, float *h, cudaStream_t st);
+                           int D, float *out, float *h, cudaStream_t st, const float *ln_w = nullptr,
+                           float eps = 0.0f, float *hn = nullptr);
 
 // y[m][o] = W[o] . x[m] for fp32 weights (matmul_f32, quant.h:117-148),
 // then (optional) + bias, and either stored, added to y (residual) or handed

@@ -233,8 +233,10 @@ void trace_row_i(pc_ctx *c, const std::string &name, const int *dev, int n) {
 
 // The MoE block of one layer for M rows whose normalized states are x:
 // router (or given routing), gate_up + SwiGLU, down, combine.
+// With next_ln set, the combine also writes c->hn = rmsnorm(h, next_ln): the
+// next layer's input norm or the final norm, saving their launches.
 pc_status run_moe(pc_ctx *c, int l, const float *x, int M, const int *sel_in, const float *w_in,
-                  int bias_first, float *out, float *h) {
+                  int bias_first, float *out, float *h, const float *next_ln = nullptr) {
     const pc_model_cfg &k = c->cfg;
     const int K = k.topk, D = k.hidden;
     Layer &ly = c->L[l];
@@ -321,7 +323,7 @@ pc_status run_moe(pc_ctx *c, int l, const float *x, int M, const int *sel_in, co
                       c->eo + ((size_t)last * K + kk) * D, D);
         }
     }
-    PC_CU(launch_combine(c->eo, c->rw, c->sel, k.routed_scale, M, K, D, out, h, c->st));
+    PC_CU(launch_combine(c->eo, c->rw, c->sel, k.routed_scale, M, K, D, out, h, c->st, next_ln, k.eps, c->hn));
     ++c->launches;
     return PC_OK;
 }
@@ -341,8 +343,10 @@ pc_status run_step(pc_ctx *c, int M, const int *seq, int lm_mode, int nsplit_ful
         Layer &ly = c->L[l];
         const std::string pre = "layer" + std::to_string(l) + ".";
         trace_row(c, pre + "input", c->h + (size_t)last * D, D);
-        PC_CU(launch_rmsnorm(c->h, ly.in_ln, c->hn, M, D, k.eps, c->st));
-        ++c->launches;
+        if (l == 0) {  // later layers get it from the previous combine
+            PC_CU(launch_rmsnorm(c->h, ly.in_ln, c->hn, M, D, k.eps, c->st));
+            ++c->launches;
+        }
         trace_row(c, pre + "pre_attn_norm", c->hn + (size_t)last * D, D);
         void *kc = c->kc[l], *vc = c->vc[l];
         if (ly.wq.t.fmt != TF_F32) {
@@ -432,12 +436,15 @@ pc_status run_step(pc_ctx *c, int M, const int *seq, int lm_mode, int nsplit_ful
         PC_CU(launch_rmsnorm(c->h, ly.post_ln, c->hn, M, D, k.eps, c->st));
         ++c->launches;
         trace_row(c, pre + "pre_moe_norm", c->hn + (size_t)last * D, D);
-        PC_TRY(run_moe(c, l, c->hn, M, nullptr, nullptr, 0, c->trace ? c->moe_out : nullptr, c->h));
+        const float *next_ln = l + 1 < k.n_layers ? c->L[l + 1].in_ln : c->final_norm;
+        PC_TRY(run_moe(c, l, c->hn, M, nullptr, nullptr, 0, c->trace ? c->moe_out : nullptr, c->h, next_ln));
         trace_row(c, pre + "moe_out", c->moe_out + (size_t)last * D, D);
         trace_row(c, pre + "output", c->h + (size_t)last * D, D);
     }
-    PC_CU(launch_rmsnorm(c->h, c->final_norm, c->hn, M, D, k.eps, c->st));
-    ++c->launches;
+    if (k.n_layers == 0) {  // otherwise the last combine wrote it
+        PC_CU(launch_rmsnorm(c->h, c->final_norm, c->hn, M, D, k.eps, c->st));
+        ++c->launches;
+    }
     trace_row(c, "final_norm", c->hn + (size_t)last * D, D);
     if (lm_mode == 2) return PC_OK;
     const int nlog = lm_mode == 1 ? 1 : M;
@@ -910,11 +917,23 @@ pc_status pc_get_logits(pc_ctx *c, int row, float *logits, int n) {
     return PC_OK;
 }
 
+// run_moe over M rows in chunks whose (row, k) pairs fit one router job table.
+pc_status run_moe_rows(pc_ctx *c, int layer, const float *x, int M, const int *sel, const float *w, float *out) {
+    const int K = c->cfg.topk, D = c->cfg.hidden;
+    const int chunk = std::max(1, GEMV_MAX_JOBS / K);
+    for (int off = 0; off < M; off += chunk) {
+        const int m = std::min(chunk, M - off);
+        PC_TRY(run_moe(c, layer, x + (size_t)off * D, m, sel ? sel + (size_t)off * K : nullptr,
+                       w ? w + (size_t)off * K : nullptr, 0, out + (size_t)off * D, nullptr));
+    }
+    return PC_OK;
+}
+
 pc_status pc_moe_layer(pc_ctx *c, int layer, const float *x_dev, float *out_dev, int M) {
     PC_TRY(check_ctx(c));
     if (layer < 0 || layer >= c->cfg.n_layers || !x_dev || !out_dev) return fail(PC_ERR_INVALID_ARG, "bad moe_layer arguments");
     if (M < 1 || M > c->maxm) return fail(PC_ERR_RANGE, "M outside [1, " + std::to_string(c->maxm) + "]");
-    PC_TRY(run_moe(c, layer, x_dev, M, nullptr, nullptr, 0, out_dev, nullptr));
+    PC_TRY(run_moe_rows(c, layer, x_dev, M, nullptr, nullptr, out_dev));
     PC_CU(cudaMemcpyAsync(c->h_err, c->err, 4, cudaMemcpyDeviceToHost, c->st));
     PC_CU(cudaStreamSynchronize(c->st));
     return check_err(c);
@@ -926,7 +945,7 @@ pc_status pc_moe_experts(pc_ctx *c, int layer, const float *x_dev, const int *se
     if (layer < 0 || layer >= c->cfg.n_layers || !x_dev || !out_dev || !sel_dev || !w_dev)
         return fail(PC_ERR_INVALID_ARG, "bad moe_experts arguments");
     if (M < 1 || M > c->maxm) return fail(PC_ERR_RANGE, "M outside [1, " + std::to_string(c->maxm) + "]");
-    PC_TRY(run_moe(c, layer, x_dev, M, sel_dev, w_dev, 0, out_dev, nullptr));
+    PC_TRY(run_moe_rows(c, layer, x_dev, M, sel_dev, w_dev, out_dev));
     PC_CU(cudaMemcpyAsync(c->h_err, c->err, 4, cudaMemcpyDeviceToHost, c->st));
     PC_CU(cudaStreamSynchronize(c->st));
     return check_err(c);
