@@ -208,6 +208,11 @@ pc_status pc_check_device(pc_ctx *ctx);
 /* Counts kernels this library launched on the context (for measurement). */
 uint64_t pc_kernel_launches(const pc_ctx *ctx);
 
+/* Smallest number of rows in one step (batch or prefill chunk) that runs the
+ * INT8 dense projections on the tensor cores, or 0 when that path is off
+ * (non-INT8 dense weights, no tensor-map encoder, or PICCHIO_TC=0). */
+int pc_tensor_core_min_rows(const pc_ctx *ctx);
+
 /* Kernel timing: between begin and end, steps run without CUDA graphs and
  * every hot-path launch is bracketed by CUDA events on the context stream;
  * pc_profile_get returns the summed duration and launch count of one label

@@ -142,6 +142,8 @@ def lib():
         L.pc_check_device.argtypes = [vp]
         L.pc_kernel_launches.argtypes = [vp]
         L.pc_kernel_launches.restype = C.c_uint64
+        L.pc_tensor_core_min_rows.argtypes = [vp]
+        L.pc_tensor_core_min_rows.restype = C.c_int
         L.pc_generate.argtypes = [vp, C.c_int, C.c_int, C.c_int, ip, fp]
         L.pc_kv_fill_synthetic.argtypes = [vp, C.c_int, C.c_int, C.c_uint64]
         L.pc_kv_fill_synthetic.restype = st
@@ -316,6 +318,11 @@ class Model:
     @property
     def launches(self) -> int:
         return int(lib().pc_kernel_launches(self._h))
+
+    @property
+    def tensor_core_min_rows(self) -> int:
+        """Rows per step from which the dense projections use the tensor cores (0: off)."""
+        return int(lib().pc_tensor_core_min_rows(self._h))
 
 
 class QT:

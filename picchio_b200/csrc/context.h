@@ -10,6 +10,7 @@
 #include "../../include/picchio_b200.h"
 #include "decode.h"
 #include "layout.h"
+#include "tcgemm.h"
 
 namespace pc {
 
@@ -112,6 +113,11 @@ struct pc_ctx {
     int *h_err = nullptr;       // pinned mirror of the device error word
     std::vector<void *> allocs; // device allocations owned by the context
     void *pinned = nullptr;     // pinned staging block
+
+    // tensor-core path for batches of rows (tcgemm.cu): state, and the INT8
+    // dense weights as row-major copies (per layer q, k, v, o; then lm_head)
+    pc::TcState tc;
+    std::vector<pc::TcWeight> tcw;
 
     // persistent decode kernel (decode.cu): 0 = not set up yet, 1 = used, -1 = not applicable
     int dec_state = 0;

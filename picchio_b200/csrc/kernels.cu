@@ -127,12 +127,14 @@ __global__ void __launch_bounds__(NORM_THREADS) rmsnorm_kernel(const float *x, c
 }
 
 // --------------------------------------------------------------- router ----
-// Dot products: four warps per expert (two experts per block), each lane
+// Dot products: four warps per expert (two experts and up to ROUTER_ROWS
+// input rows per block, rows spread over blockIdx.y), each lane
 // with all of its 16-byte loads of R and x in flight at once; the quarters
 // are added in a fixed order.  The last block to finish (atomic ticket) does
 // the top-k, the softmax and the expert job tables, reading the selection
 // from shared memory.
-constexpr int ROUTER_RV = 6;  // float4 per lane per operand in flight
+constexpr int ROUTER_RV = 6;    // float4 per lane per operand in flight
+constexpr int ROUTER_ROWS = 2;  // input rows per block (blockIdx.y = row group)
 
 __global__ void __launch_bounds__(256) router_kernel(const RouterParams r) {
     pdl_wait();
@@ -146,7 +148,8 @@ __global__ void __launch_bounds__(256) router_kernel(const RouterParams r) {
     if (!r.sel_in) {
         const int e = blockIdx.x * 2 + (warp >> 2), q = warp & 3;
         const bool vec = (r.D & 3) == 0;
-        for (int m = 0; m < r.M; ++m) {
+        const int m1 = min(r.M, (int)(blockIdx.y + 1) * ROUTER_ROWS);
+        for (int m = blockIdx.y * ROUTER_ROWS; m < m1; ++m) {
             float s = 0.0f;
             if (e < r.E) {
                 const float *re = r.R + (int64_t)e * r.D;
@@ -196,7 +199,7 @@ __global__ void __launch_bounds__(256) router_kernel(const RouterParams r) {
         }
         __threadfence();
         if (threadIdx.x == 0) {
-            last = atomicAdd(r.counter, 1u) == gridDim.x - 1;
+            last = atomicAdd(r.counter, 1u) == gridDim.x * gridDim.y - 1;
             if (last) *r.counter = 0u;
         }
         __syncthreads();
@@ -256,14 +259,15 @@ __global__ void __launch_bounds__(256) router_kernel(const RouterParams r) {
         }
         __syncthreads();
     }
-    // expert job tables: pairs grouped by expert, at most 8 pairs per job
+    // expert job tables: pairs grouped by expert, at most pj pairs per job
     const int Ps = min(P, GEMV_MAX_JOBS);
+    const int pj = (r.per_job > 0 && r.per_job < GEMV_MAXR) ? r.per_job : GEMV_MAXR;
     const int e = threadIdx.x;
     int n = 0;
     if (e < r.E && e >= r.e_lo && e < r.e_hi) {
         for (int p = 0; p < Ps; ++p) n += (ssel[p] == e);
     }
-    cnt[e] = (n + GEMV_MAXR - 1) / GEMV_MAXR;
+    cnt[e] = (n + pj - 1) / pj;
     __syncthreads();
     if (warp == 0) {  // exclusive scan of jobs per expert: 8 experts per lane
         int v[8], tot = 0;
@@ -312,7 +316,7 @@ __global__ void __launch_bounds__(256) router_kernel(const RouterParams r) {
         dn.out_row[fill] = p;
         ++fill;
         gu.nrows = dn.nrows = fill;
-        if (fill == GEMV_MAXR) { fill = 0; ++j; }
+        if (fill == pj) { fill = 0; ++j; }
     }
 }
 
@@ -531,8 +535,8 @@ cudaError_t launch_rmsnorm(const float *x, const float *w, float *out, int M, in
 
 cudaError_t launch_router(const RouterParams &r, cudaStream_t st) {
     if (r.E > 256 || r.K > 16 || r.M * r.K > GEMV_MAX_JOBS) return cudaErrorInvalidValue;
-    const int blocks = r.sel_in ? 1 : (r.E + 1) / 2;
-    return launch_k(router_kernel, dim3(blocks), dim3(256), 0, st, r);
+    const dim3 grid = r.sel_in ? dim3(1) : dim3((r.E + 1) / 2, (r.M + ROUTER_ROWS - 1) / ROUTER_ROWS);
+    return launch_k(router_kernel, grid, dim3(256), 0, st, r);
     return cudaGetLastError();
 }
 

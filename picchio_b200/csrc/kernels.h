@@ -58,6 +58,7 @@ struct RouterParams {
     int e_lo, e_hi;        // experts resident here (expert parallelism)
     int *slot_of;          // optional [E] HBM slot of each expert (streamed residency) or null
     GemvJob *jobs_gu, *jobs_dn;
+    int per_job;           // (row, k) pairs per job, 1..GEMV_MAXR (0 = GEMV_MAXR)
     int *njobs;            // [2]: gate_up, down
     int *pair_local;       // [M*K] 1 if the pair's expert is resident here
 };

@@ -54,6 +54,7 @@ pc_status device_setup(int dev, int *nsm, int *max_smem) {
     if (dev >= 0 && dev < 64 && !g_configured[dev]) {
         PC_CU(gemv_configure(*max_smem));
         PC_CU(decode_configure(*max_smem));
+        PC_CU(tc_configure());
         g_configured[dev] = true;
     }
     return PC_OK;
@@ -214,6 +215,64 @@ void use_jobs(GemvParams &p, const DenseJobs *dj, int off, int cnt_idx) {
 // Launches with at most 8 input rows keep them all in the B operand.
 int shared_rows_for(int rows) { return rows <= GEMV_MAXR ? rows : 0; }
 
+bool use_tc(const pc_ctx *c, int M) { return c->tc.on && M >= TC_MIN_ROWS && M <= TC_MAX_ROWS; }
+
+// The dense projection described by g (epilogue fields set as for the GEMV)
+// over input rows 0..M-1 on the tensor cores: the rows' digit planes, then one
+// launch over the nseg weight matrices (q, k, v or a single one).
+pc_status run_tc(pc_ctx *c, const GemvParams &g, const TcWeight *const *w, const float *const *bias, int nseg, int M,
+                 const char *label) {
+    TcParams t;
+    memset(&t, 0, sizeof t);
+    int tiles = 0;
+    for (int s = 0; s < nseg; ++s) {
+        t.segs[s].amap = w[s]->map;
+        t.segs[s].rs = w[s]->rs;
+        t.segs[s].bias = bias[s];
+        t.segs[s].O = w[s]->O;
+        t.segs[s].Op = w[s]->Op;
+        t.segs[s].seg = s;
+        t.tile_base[s] = tiles;
+        tiles += (w[s]->Op + 127) / 128;
+    }
+    t.nseg = nseg;
+    t.tile_base[nseg] = tiles;
+    t.ksteps = (w[0]->Ip + 127) / 128;
+    t.nsplit = tc_nsplit(tiles, t.ksteps, c->nsm);
+    if (tc_part_bytes(tiles, t.nsplit, M) > c->tc.part_bytes || tiles > c->tc.ctr_n) t.nsplit = 1;
+    t.bmap = c->tc.bmap[M <= 32 ? 0 : M <= 64 ? 1 : 2];
+    t.Mpad = c->tc.Mpad;
+    t.inv = c->tc.inv;
+    t.part = c->tc.part;
+    t.ctr = c->tc.ctr;
+    t.err = c->err;
+    t.epi = g.epi;
+    t.perm = g.perm;
+    t.head_dim = g.head_dim;
+    t.y = g.y;
+    t.ldy = g.ldy;
+    t.residual = g.residual;
+    t.res_src = g.res_src;
+    t.rope_cs = g.rope_cs;
+    t.rope_sn = g.rope_sn;
+    t.row_pos = g.row_pos;
+    t.row_seq = g.row_seq;
+    t.qbuf = g.qbuf;
+    t.ldq = g.ldq;
+    t.kcache = g.kcache;
+    t.vcache = g.vcache;
+    t.kv_bf16 = g.kv_bf16;
+    t.kv_seq_stride = g.kv_seq_stride;
+    t.kv_ctx = g.kv_ctx;
+    t.kv_dim = g.kv_dim;
+    t.argmax = g.argmax;
+    Prof pr(c, label);
+    PC_CU(tc_prep_rows(c->tc, g.x, g.ldx, M, g.I, c->st));
+    PC_CU(tc_launch(t, M, c->st));
+    c->launches += 2;
+    return PC_OK;
+}
+
 void trace_row(pc_ctx *c, const std::string &name, const float *dev, int n) {
     if (!c->trace) return;
     std::vector<float> v(n);
@@ -272,6 +331,12 @@ pc_status run_moe(pc_ctx *c, int l, const float *x, int M, const int *sel_in, co
     r.slot_of = nullptr;
     r.jobs_gu = c->jobs_gu;
     r.jobs_dn = c->jobs_dn;
+    // Many rows but few pairs per expert (batched decode, ~2 per expert):
+    // jobs of at most 4 pairs keep the expert GEMVs on two N-tiles with
+    // deeper weight rings than 8-pair jobs (an expert with more pairs is
+    // streamed once per job).  Otherwise up to GEMV_MAXR pairs per job; with
+    // M <= GEMV_MAXR the B operand holds all M token rows (shared_rows below).
+    r.per_job = (M > GEMV_MAXR && (int64_t)M * K <= 3LL * k.n_experts) ? 4 : GEMV_MAXR;
     r.njobs = c->njobs;
     r.pair_local = c->pair_local;
     {
@@ -285,7 +350,7 @@ pc_status run_moe(pc_ctx *c, int l, const float *x, int M, const int *sel_in, co
         trace_row_i(c, "layer" + std::to_string(l) + ".top_indices", c->sel + (size_t)last * K, K);
         trace_row(c, "layer" + std::to_string(l) + ".top_weights", c->rw + (size_t)last * K, K);
     }
-    const int rows = std::min(M, GEMV_MAXR);
+    const int rows = std::min(M, r.per_job);
     GemvParams p{};
     params_for(p, c->eg.gu, EPI_SWIGLU);
     p.static_jobs = 0;  // written by the router kernel
@@ -368,7 +433,13 @@ pc_status run_step(pc_ctx *c, int M, const int *seq, int lm_mode, int nsplit_ful
             p.kv_seq_stride = c->seq_stride;
             p.kv_ctx = c->kv_ctx;
             p.kv_dim = KVH * hd;
-            PC_TRY(run_gemv(c, p, std::min(M, GEMV_MAXR), "qkv"));
+            if (use_tc(c, M)) {
+                const TcWeight *w[3] = {&c->tcw[4 * l], &c->tcw[4 * l + 1], &c->tcw[4 * l + 2]};
+                const float *b[3] = {ly.wq.bias, ly.wk.bias, ly.wv.bias};
+                PC_TRY(run_tc(c, p, w, b, 3, M, "qkv"));
+            } else {
+                PC_TRY(run_gemv(c, p, std::min(M, GEMV_MAXR), "qkv"));
+            }
         } else {
             const int Oq = H * hd, Ok = KVH * hd, ldr = Oq + 2 * Ok;
             F32GemvParams f{};
@@ -414,7 +485,13 @@ pc_status run_step(pc_ctx *c, int M, const int *seq, int lm_mode, int nsplit_ful
             p.y = ydst;
             p.ldy = D;
             p.residual = c->trace ? 0 : 1;
-            PC_TRY(run_gemv(c, p, std::min(M, GEMV_MAXR), "o_proj"));
+            if (use_tc(c, M)) {
+                const TcWeight *w[1] = {&c->tcw[4 * l + 3]};
+                const float *b[1] = {ly.wo.bias};
+                PC_TRY(run_tc(c, p, w, b, 1, M, "o_proj"));
+            } else {
+                PC_TRY(run_gemv(c, p, std::min(M, GEMV_MAXR), "o_proj"));
+            }
         } else {
             F32GemvParams f{};
             f.W = ly.wo.t.f32; f.O = D; f.I = H * hd; f.x = c->attn; f.ldx = H * hd; f.M = M;
@@ -458,7 +535,13 @@ pc_status run_step(pc_ctx *c, int M, const int *seq, int lm_mode, int nsplit_ful
         p.y = c->logits;
         p.ldy = k.vocab;
         p.argmax = c->argmax;
-        PC_TRY(run_gemv(c, p, std::min(M, GEMV_MAXR), "lm_head"));
+        if (nlog == M && use_tc(c, M)) {
+            const TcWeight *w[1] = {&c->tcw.back()};
+            const float *b[1] = {nullptr};
+            PC_TRY(run_tc(c, p, w, b, 1, M, "lm_head"));
+        } else {
+            PC_TRY(run_gemv(c, p, std::min(M, GEMV_MAXR), "lm_head"));
+        }
     } else {
         F32GemvParams f{};
         f.W = c->lm_head.t.f32; f.O = k.vocab; f.I = D; f.x = c->hn + (size_t)(lm_mode == 1 ? M - 1 : 0) * D;
@@ -757,8 +840,58 @@ pc_status make_ctx(const pc_opts *opts, pc_ctx **out) {
     return PC_OK;
 }
 
+// The tensor-core path for batches of 16..128 rows (tcgemm.cu): row-major
+// copies of every INT8 dense projection and the shared digit / partial-sum
+// buffers.  Off when a dense projection is not INT8, when the driver's
+// tensor-map encoder is unavailable, or with PICCHIO_TC=0.
+pc_status tc_setup(pc_ctx *c) {
+    const char *v = getenv("PICCHIO_TC");
+    if ((v && v[0] == '0') || !tc_driver_ready() || c->L.empty()) return PC_OK;
+    bool ok = c->lm_head.t.fmt == TF_T8;
+    for (auto &ly : c->L)
+        ok = ok && ly.wq.t.fmt == TF_T8 && ly.wk.t.fmt == TF_T8 && ly.wv.t.fmt == TF_T8 && ly.wo.t.fmt == TF_T8 &&
+             ly.wk.t.perm == ly.wq.t.perm && ly.wv.t.perm == ly.wq.t.perm;
+    if (!ok) return PC_OK;
+    const int rows = std::min(c->maxm, TC_MAX_ROWS);
+    size_t part = 16;
+    int max_tiles = 1, max_kp = 0;
+    auto need = [&](std::initializer_list<const TileDesc *> ts) {
+        int tiles = 0, ip = 0;
+        for (const TileDesc *t : ts) { tiles += (t->Op + 127) / 128; ip = t->Ip; }
+        const int ks = (ip + 127) / 128;
+        part = std::max(part, tc_part_bytes(tiles, tc_nsplit(tiles, ks, c->nsm), rows));
+        max_tiles = std::max(max_tiles, tiles);
+        max_kp = std::max(max_kp, ip);
+    };
+    need({&c->L[0].wq.t, &c->L[0].wk.t, &c->L[0].wv.t});
+    need({&c->L[0].wo.t});
+    need({&c->lm_head.t});
+    c->tcw.assign(4 * c->L.size() + 1, TcWeight{});
+    for (size_t l = 0; l < c->L.size(); ++l) {
+        const TileDesc *ts[4] = {&c->L[l].wq.t, &c->L[l].wk.t, &c->L[l].wv.t, &c->L[l].wo.t};
+        for (int i = 0; i < 4; ++i) {
+            TcWeight &w = c->tcw[4 * l + i];
+            cudaError_t e = tc_weight_from_tiles(*ts[i], w, c->st);
+            if (w.q) c->allocs.push_back(w.q);
+            if (e != cudaSuccess) return cuda_fail(e, "tc_weight_from_tiles");
+        }
+    }
+    TcWeight &lm = c->tcw.back();
+    cudaError_t e = tc_weight_from_tiles(c->lm_head.t, lm, c->st);
+    if (lm.q) c->allocs.push_back(lm.q);
+    if (e != cudaSuccess) return cuda_fail(e, "tc_weight_from_tiles");
+    e = tc_state_init(c->tc, rows, max_kp, part, max_tiles);
+    for (void *p : {(void *)c->tc.dig, (void *)c->tc.inv, (void *)c->tc.part, (void *)c->tc.ctr})
+        if (p) c->allocs.push_back(p);
+    if (e != cudaSuccess) return cuda_fail(e, "tc_state_init");
+    PC_CU(cudaStreamSynchronize(c->st));
+    c->tc.on = true;
+    return PC_OK;
+}
+
 pc_status finish_init(pc_ctx *c) {
     if (c->opts.ep_size > 1) PC_TRY(ep_init(c));
+    PC_TRY(tc_setup(c));
     return PC_OK;
 }
 
@@ -1007,6 +1140,8 @@ pc_status pc_check_device(pc_ctx *c) {
 }
 
 uint64_t pc_kernel_launches(const pc_ctx *c) { return c ? c->launches : 0; }
+
+int pc_tensor_core_min_rows(const pc_ctx *c) { return (c && c->tc.on) ? TC_MIN_ROWS : 0; }
 
 pc_status pc_generate(pc_ctx *c, int tok, int pos, int n, int *out_ids, float *device_ms) {
     PC_TRY(check_ctx(c));

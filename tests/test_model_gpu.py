@@ -122,6 +122,37 @@ def test_decode_batch_matches_single_sequences(variant):
             assert outs[i] == singles[i][:6] or outs[i][:len(singles[i])] == singles[i][:len(outs[i])]
 
 
+def test_decode_batch_tensor_core_rows(variant):
+    """18 sequences in one batch: q/k/v, o_proj and the lm_head of every step
+    take the tensor-core path (16..128 rows); each sequence's greedy ids match
+    the same sequence decoded alone (batch 1: the GEMV path)."""
+    from picchio_b200 import Model
+    m, d = variant
+    B, steps = 18, 4
+    prompts = [m["prompt"][i:i + 3] for i in range(B)]
+    singles = []
+    for p in prompts[:4]:
+        with Model(d, ctx=m["ctx"]) as s:
+            singles.append(s.generate(p, steps))
+    with Model(d, ctx=m["ctx"], max_batch=B) as b:
+        # the path is on exactly when the dense projections are INT8
+        assert b.tensor_core_min_rows == (16 if m["name"].endswith("_i8") else 0)
+        cur = [p[0] for p in prompts]
+        pos = [0] * B
+        outs = [[] for _ in range(B)]
+        for step in range(3 + steps - 1):
+            nxt = b.decode_batch(cur, pos)
+            for i, p in enumerate(prompts):
+                pos[i] += 1
+                if pos[i] < len(p):
+                    cur[i] = p[pos[i]]
+                else:
+                    outs[i].append(nxt[i])
+                    cur[i] = nxt[i]
+        for i in range(4):
+            assert outs[i] == singles[i][:len(outs[i])], (i, outs[i], singles[i])
+
+
 def test_moe_forward_against_oracle(variant):
     import torch
     from picchio_b200 import Model
@@ -129,13 +160,17 @@ def test_moe_forward_against_oracle(variant):
     orc = O.OracleModel(d, ctx=64)
     rng = np.random.default_rng(3)
     D = orc.c.hidden
-    x = rng.standard_normal((5, D)).astype(np.float32)
-    with Model(d, ctx=64) as model:
-        for layer in range(orc.c.n_layers):
-            out = model.moe_forward(torch.from_numpy(x).cuda(), layer).cpu().numpy()
-            for r in range(5):
-                ref = orc.moe(x[r], layer)
-                assert rel_l2(out[r], ref) < 1e-5, (layer, r)
+    # 5 rows: all rows in one shared B operand; 12 rows: more than one job
+    # table row group with at most 2 pairs per expert job (batched-decode
+    # form); 40 rows: up to 8 pairs per job
+    for M in (5, 12, 40):
+        x = rng.standard_normal((M, D)).astype(np.float32)
+        with Model(d, ctx=64, max_batch=64) as model:
+            for layer in range(orc.c.n_layers):
+                out = model.moe_forward(torch.from_numpy(x).cuda(), layer).cpu().numpy()
+                for r in range(M):
+                    ref = orc.moe(x[r], layer)
+                    assert rel_l2(out[r], ref) < 1e-5, (M, layer, r)
 
 
 def test_range_errors(variant):
@@ -199,3 +234,24 @@ def test_persistent_decode_kernel_matches_reference(monkeypatch):
         tok = model.prefill_tokens(m["prompt"], 0)
         dev, _ = model.generate_device(tok, n, 32)
         assert [tok] + dev[:31] == m["ids_batched"][:32]
+
+
+def test_tensor_core_split_k_prefill_matches_sequential():
+    """A model wide enough that the tensor-core projections split K over
+    several CTAs per 128-row tile (d_model 1024: 8 steps of 128 columns):
+    a 24-token prefill (tensor-core path) gives the logits and next id of 24
+    sequential single-token forwards (GEMV path).  The tensor-core sums are
+    exact integers rounded once, the GEMV's are rounded per 256 columns, so
+    the two agree to ~1e-6."""
+    from picchio_b200 import Model, ModelConfig
+    cfg = ModelConfig(hidden=1024, n_layers=2, n_heads=16, n_kv_heads=4, head_dim=64, n_experts=8, topk=2,
+                      intermediate=512, vocab=2048)
+    prompt = [int(v) for v in np.random.default_rng(5).integers(0, 2048, 24)]
+    with Model.synthetic(cfg, seed=3, ctx=64) as a, Model.synthetic(cfg, seed=3, ctx=64) as b:
+        assert a.tensor_core_min_rows == 16  # the path under test is on
+        t1 = a.prefill_tokens(prompt, 0)
+        t2 = None
+        for i, t in enumerate(prompt):
+            t2 = b.forward_token(t, i)
+        assert t1 == t2
+        assert rel_l2(a.logits(0), b.logits(0)) < 1e-5
