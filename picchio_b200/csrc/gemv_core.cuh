@@ -10,8 +10,9 @@
 //  * weights go straight from HBM into registers: per step (up to 4 T4 or 8
 //    T8 k-blocks of one unit) every lane loads its 16-byte A fragment of each
 //    block and its rows' group scales, one step ahead of the step it computes;
-//    HBM latency is covered by L2 prefetches of the warp's slices of its next
-//    units (up to ~288 KB per SM), which hold no registers or shared memory;
+//    HBM latency is covered by L2 prefetches (one bulk request per slice) of
+//    the warp's slices of its next units (up to ~288 KB per SM), which hold
+//    no registers or shared memory;
 //  * the MMAs are s8 x s8 -> s32 m16n8k32: a nibble n becomes the signed byte
 //    16 (n - 8) in one or two logic ops, INT8 weights need nothing;
 //  * the input rows are scaled by a power of two, rounded to 22-bit integers
@@ -620,12 +621,9 @@ __device__ __forceinline__ void gemv_cta(const GemvParams &p, uint8_t *smem, int
     const int PD = max(1, min(ntot, PREFETCH_BYTES / NCONS / max(1, need * BB)));
     int pf_u, pf_j;
     first_from(j0, pf_u, pf_j);
-    auto prefetch_next = [&]() {
+    auto prefetch_next = [&]() {  // one bulk request per slice (block bytes are multiples of 16)
         if (pf_u < u1 && nbw > 0) {
-            const uintptr_t a0 = reinterpret_cast<uintptr_t>(slice(pf_u, pf_j));
-            const uintptr_t a1 = a0 + (uintptr_t)nbw * BB;
-            for (uintptr_t a = (a0 & ~(uintptr_t)127) + lane * 128; a < a1; a += 32 * 128)
-                prefetch_l2(reinterpret_cast<const void *>(a));
+            if (lane == 0) bulk_prefetch_l2(slice(pf_u, pf_j), (uint32_t)(nbw * BB));
             advance(pf_u, pf_j);
         }
     };

@@ -84,6 +84,11 @@ __device__ __forceinline__ void cp_async_wait() {
 }
 
 // Brings the 128-byte line holding p into L2; nothing waits for it.
+// Asks L2 for `bytes` bytes at p (16-byte aligned, a multiple of 16) with one
+// bulk request; no data is returned to the SM.
+__device__ __forceinline__ void bulk_prefetch_l2(const void *p, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
 __device__ __forceinline__ void prefetch_l2(const void *p) {
     asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
 }

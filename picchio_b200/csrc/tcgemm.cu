@@ -43,74 +43,108 @@ struct TcCfg {
     static constexpr int B = N * 128;            // one digit plane's box bytes
     static constexpr int STAGE = A + 3 * B;
     static constexpr int TCOLS = 3 * N <= 128 ? 128 : 3 * N <= 256 ? 256 : 512;  // TMEM columns
-    static constexpr int SMEM = 1024 + S * STAGE + 256;
+    static constexpr int SMEM = 1024 + S * STAGE + 256 + 12 * N;  // + barriers, + per-column operands
 };
 
 __device__ __forceinline__ void tc_fail(int *err, int code) {
     if (err) atomicCAS(err, 0, code);
 }
 
-// One column (input row n) of one weight row: epilogue of the three digit
-// sums.  All 32 lanes of the warp call this together (QKV pairs rows through
-// a shuffle).
-__device__ __forceinline__ void tc_finish64(const TcParams &p, const TcSeg &sg, int n, int o, bool rv, float rs,
-                                            float bias, int tr16, int o_lo, long long s64) {
-    const bool live = rv && n < p.M;
-    float x = __fmul_rn(__ll2float_rn(s64), live ? p.inv[n] : 0.0f);
-    if (sg.rs) x = __fmul_rn(x, rs);
-    if (sg.bias) x = __fadd_rn(x, bias);
+// Epilogue of 16 columns (input rows c0..c0+15) of one weight row (this
+// thread's TMEM lane): s[j] is the row's exact dot with input row c0 + j in
+// units of 2^-sh.  Every global operand of the 16 columns is loaded before
+// any is used; the per-column ones (2^-sh, position, sequence slot) come from
+// shared memory.  All 32 lanes of the warp call this together (QKV pairs rows
+// g and g + 8 of a 16-row tile through a shuffle; LOGITS reduces over rows).
+__device__ __forceinline__ void tc_epi16(const TcParams &p, const TcSeg &sg, int c0, const long long (&s)[16], int o,
+                                         bool rv, float rs, float bias, int tr16, int o_lo, const float *cinv,
+                                         const int *cpos, const int *cseq) {
+    float x[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+        float v = __fmul_rn(__ll2float_rn(s[j]), cinv[c0 + j]);
+        if (sg.rs) v = __fmul_rn(v, rs);
+        if (sg.bias) v = __fadd_rn(v, bias);
+        x[j] = v;
+    }
     if (p.epi == EPI_QKV) {
-        const float other = __shfl_xor_sync(0xffffffffu, x, 8);
         const bool is_lo = (tr16 & 8) == 0;
-        const bool pair_ok = __shfl_xor_sync(0xffffffffu, (int)rv, 8) != 0 && rv;
-        if (!(live && pair_ok)) return;
-        float lo = is_lo ? x : other, hi = is_lo ? other : x;
-        const int pos = p.row_pos[n];
-        if (sg.seg != 2) {
-            // rope_apply (picchio.c:467-469) rounded as the reference build does
-            const int half = p.head_dim >> 1, j = o_lo % p.head_dim;
-            const float cs = p.rope_cs[(int64_t)pos * half + j], sn = p.rope_sn[(int64_t)pos * half + j];
-            const float a = lo, b = hi;
-            lo = __fmaf_rn(a, cs, -__fmul_rn(b, sn));
-            hi = __fmaf_rn(a, sn, __fmul_rn(b, cs));
+        const bool pair_ok = rv && __shfl_xor_sync(0xffffffffu, (int)rv, 8) != 0;
+        float oth[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) oth[j] = __shfl_xor_sync(0xffffffffu, x[j], 8);
+        if (!pair_ok) return;
+        const int half = p.head_dim >> 1, jj = o_lo % p.head_dim;
+        float cs[16], sn[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+            cs[j] = 1.0f;
+            sn[j] = 0.0f;
+            const int n = c0 + j;
+            if (sg.seg != 2 && n < p.M) {
+                const int64_t at = (int64_t)cpos[n] * half + jj;
+                cs[j] = p.rope_cs[at];
+                sn[j] = p.rope_sn[at];
+            }
         }
-        const float val = is_lo ? lo : hi;
-        if (sg.seg == 0) {
-            p.qbuf[(int64_t)n * p.ldq + o] = val;
-        } else if (pos >= 0 && pos < p.kv_ctx) {  // kv_store drops pos >= max_pos (picchio.c:495)
-            const int64_t at = (int64_t)p.row_seq[n] * p.kv_seq_stride + (int64_t)pos * p.kv_dim + o;
-            void *cache = sg.seg == 1 ? p.kcache : p.vcache;
-            if (p.kv_bf16)
-                reinterpret_cast<__nv_bfloat16 *>(cache)[at] = __float2bfloat16_rn(val);
-            else
-                reinterpret_cast<float *>(cache)[at] = val;
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+            const int n = c0 + j;
+            if (n >= p.M) continue;
+            float lo = is_lo ? x[j] : oth[j], hi = is_lo ? oth[j] : x[j];
+            if (sg.seg != 2) {
+                // rope_apply (picchio.c:467-469) rounded as the reference build does
+                const float a = lo, b = hi;
+                lo = __fmaf_rn(a, cs[j], -__fmul_rn(b, sn[j]));
+                hi = __fmaf_rn(a, sn[j], __fmul_rn(b, cs[j]));
+            }
+            const float val = is_lo ? lo : hi;
+            const int pos = cpos[n];
+            if (sg.seg == 0) {
+                p.qbuf[(int64_t)n * p.ldq + o] = val;
+            } else if (pos >= 0 && pos < p.kv_ctx) {  // kv_store drops pos >= max_pos (picchio.c:495)
+                const int64_t at = (int64_t)cseq[n] * p.kv_seq_stride + (int64_t)pos * p.kv_dim + o;
+                void *cache = sg.seg == 1 ? p.kcache : p.vcache;
+                if (p.kv_bf16)
+                    reinterpret_cast<__nv_bfloat16 *>(cache)[at] = __float2bfloat16_rn(val);
+                else
+                    reinterpret_cast<float *>(cache)[at] = val;
+            }
         }
         return;
     }
     if (p.epi == EPI_LOGITS) {
-        unsigned long long key = 0ull;
-        if (live) {
-            p.y[(int64_t)n * p.ldy + o] = x;
-            key = argmax_key(x, o);
-        }
 #pragma unroll
-        for (int s = 16; s > 0; s >>= 1) {
-            const unsigned long long ot = __shfl_xor_sync(0xffffffffu, key, s);
-            key = ot > key ? ot : key;
+        for (int j = 0; j < 16; ++j) {
+            const int n = c0 + j;
+            const bool live = rv && n < p.M;
+            unsigned long long key = 0ull;
+            if (live) {
+                p.y[(int64_t)n * p.ldy + o] = x[j];
+                key = argmax_key(x[j], o);
+            }
+#pragma unroll
+            for (int m = 16; m > 0; m >>= 1) {
+                const unsigned long long ot = __shfl_xor_sync(0xffffffffu, key, m);
+                key = ot > key ? ot : key;
+            }
+            if ((threadIdx.x & 31) == 0 && n < p.M && key) atomicMax(p.argmax + n, key);
         }
-        if ((threadIdx.x & 31) == 0 && n < p.M && key) atomicMax(p.argmax + n, key);
         return;
     }
-    if (!live) return;  // EPI_STORE
-    float *dst = p.y + (int64_t)n * p.ldy + o;
-    if (p.residual) x = __fadd_rn((p.res_src ? p.res_src : p.y)[(int64_t)n * p.ldy + o], x);
-    *dst = x;
-}
-
-__device__ __forceinline__ void tc_finish(const TcParams &p, const TcSeg &sg, int n, int o, bool rv, float rs,
-                                          float bias, int tr16, int o_lo, int32_t a0, int32_t a1, int32_t a2) {
-    tc_finish64(p, sg, n, o, rv, rs, bias, tr16, o_lo,
-                (long long)a0 * 65536 + (long long)a1 * 256 + (long long)a2);
+    // EPI_STORE, optionally onto the residual
+    if (!rv) return;
+    if (p.residual) {
+        const float *src = p.res_src ? p.res_src : p.y;
+        float r[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) r[j] = c0 + j < p.M ? src[(int64_t)(c0 + j) * p.ldy + o] : 0.0f;
+#pragma unroll
+        for (int j = 0; j < 16; ++j) x[j] = __fadd_rn(r[j], x[j]);
+    }
+#pragma unroll
+    for (int j = 0; j < 16; ++j)
+        if (c0 + j < p.M) p.y[(int64_t)(c0 + j) * p.ldy + o] = x[j];
 }
 
 template <int N>
@@ -123,6 +157,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(const __grid_con
     uint64_t *accf = empty + C::S;
     uint32_t *tslot = reinterpret_cast<uint32_t *>(accf + 1);
     int *lastf = reinterpret_cast<int *>(tslot + 1);
+    float *cinv = reinterpret_cast<float *>(smem + C::S * C::STAGE + 256);  // per-column operands
+    int *cpos = reinterpret_cast<int *>(cinv + N);
+    int *cseq = cpos + N;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int tile = blockIdx.x / p.nsplit, split = blockIdx.x % p.nsplit;
     int si = 0;
@@ -211,13 +248,19 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(const __grid_con
         }
     } else {  // epilogue: warps 2..5, thread = TMEM lane = weight row of the tile
         pdl_wait();
-        const int q = warp & 3, tr = 32 * q + lane;
+        const int q = warp & 3, tr = 32 * q + lane, e = threadIdx.x - 64;
         const int prow = row0 + tr, rt = prow >> 4, tr16 = prow & 15;
         const int o = tile_row_to_logical(p.perm, p.head_dim, rt, tr16);
         const int o_lo = tile_row_to_logical(p.perm, p.head_dim, rt, tr16 & 7);
         const bool rv = prow < sg.Op && o < sg.O;
         const float rs = (rv && sg.rs) ? sg.rs[o] : 1.0f;
         const float bias = (rv && sg.bias) ? sg.bias[o] : 0.0f;
+        if (e < N) {  // per-column operands, once per CTA
+            cinv[e] = e < p.M ? p.inv[e] : 0.0f;
+            cpos[e] = (p.epi == EPI_QKV && e < p.M) ? p.row_pos[e] : 0;
+            cseq[e] = (p.epi == EPI_QKV && e < p.M) ? p.row_seq[e] : 0;
+        }
+        named_bar_sync(1, 128);
         if (!mbar_wait(accf, 0, TC_WAIT_NS)) tc_fail(p.err, 3);
         __syncwarp();
         tc_fence_after();
@@ -231,24 +274,21 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(const __grid_con
             tmem_ld16(tl + N + c0, d1);
             tmem_ld16(tl + 2 * N + c0, d2);
             tmem_ld_wait();
+            long long v[16];
+#pragma unroll
+            for (int j = 0; j < 16; ++j)
+                v[j] = (long long)(int32_t)d0[j] * 65536 + (long long)(int32_t)d1[j] * 256 + (long long)(int32_t)d2[j];
             if (p.nsplit > 1) {
 #pragma unroll
-                for (int j = 0; j < 16; ++j) {
-                    const long long v = (long long)(int32_t)d0[j] * 65536 + (long long)(int32_t)d1[j] * 256 +
-                                        (long long)(int32_t)d2[j];
-                    atomicAdd(acc + (size_t)(c0 + j) * 128 + tr, (unsigned long long)v);
-                }
+                for (int j = 0; j < 16; ++j) atomicAdd(acc + (size_t)(c0 + j) * 128 + tr, (unsigned long long)v[j]);
             } else {
-#pragma unroll
-                for (int j = 0; j < 16; ++j)
-                    tc_finish(p, sg, c0 + j, o, rv, rs, bias, tr16, o_lo, (int32_t)d0[j], (int32_t)d1[j],
-                              (int32_t)d2[j]);
+                tc_epi16(p, sg, c0, v, o, rv, rs, bias, tr16, o_lo, cinv, cpos, cseq);
             }
         }
         if (p.nsplit > 1) {
             __threadfence();
             named_bar_sync(1, 128);
-            if (threadIdx.x == 64) {
+            if (e == 0) {
                 const unsigned t = atomicAdd(p.ctr + tile, 1u);
                 *lastf = t == (unsigned)(p.nsplit - 1);
                 if (*lastf) p.ctr[tile] = 0u;
@@ -261,10 +301,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(const __grid_con
 #pragma unroll
                     for (int j = 0; j < 16; ++j) v[j] = (long long)__ldcg(acc + (size_t)(c0 + j) * 128 + tr);
 #pragma unroll
-                    for (int j = 0; j < 16; ++j) {
-                        acc[(size_t)(c0 + j) * 128 + tr] = 0ull;  // ready for the next launch
-                        tc_finish64(p, sg, c0 + j, o, rv, rs, bias, tr16, o_lo, v[j]);
-                    }
+                    for (int j = 0; j < 16; ++j) acc[(size_t)(c0 + j) * 128 + tr] = 0ull;  // ready for the next launch
+                    tc_epi16(p, sg, c0, v, o, rv, rs, bias, tr16, o_lo, cinv, cpos, cseq);
                 }
             }
         }
