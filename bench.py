@@ -17,8 +17,9 @@ full forward at positions 4096+.
   token + position, D2H of the next id + the error word inside the timed
   region), host clock.
 * roofline: the expert gate_up GEMV (the largest kernel) timed with CUDA
-  events in profiling steps; algorithmic bytes per launch = 4 experts x
-  (gate_up tiles + gate_up bias).
+  events around each launch in profiling steps (each step a one-off graph,
+  so the events see device time only, with no overlap between kernels);
+  algorithmic bytes per launch = 4 experts x (gate_up tiles + gate_up bias).
 * cpu_baseline / --impl reference: the reference's own decode functions
   (oracle/_ref) on this host's cores, see oracle/cpu_baseline.py.
 
@@ -326,7 +327,8 @@ def main():
     e2e_s = allmax(time.perf_counter() - t1, world)
     e2e = args.steps / e2e_s
 
-    # kernel timing for the roofline (profiling steps, no graphs)
+    # kernel timing for the roofline: profiling steps, each captured into a
+    # one-off graph with CUDA events around every launch (device time only)
     m.profile_begin()
     for _ in range(3):
         tok = m.forward_token(tok, pos)

@@ -213,8 +213,12 @@ uint64_t pc_kernel_launches(const pc_ctx *ctx);
  * (non-INT8 dense weights, no tensor-map encoder, or PICCHIO_TC=0). */
 int pc_tensor_core_min_rows(const pc_ctx *ctx);
 
-/* Kernel timing: between begin and end, steps run without CUDA graphs and
- * every hot-path launch is bracketed by CUDA events on the context stream;
+/* Kernel timing: between begin and end, every hot-path launch is bracketed by
+ * CUDA events on the context stream.  With graphs enabled each step is
+ * captured into a one-off graph (the events become graph nodes), so the
+ * events time the device only, free of host launch gaps; kernels then do not
+ * overlap one another across the events.  Without graphs the step is issued
+ * launch by launch.
  * pc_profile_get returns the summed duration and launch count of one label
  * ("expert_gate_up", "expert_down", "qkv", "o_proj", "lm_head",
  * "attention", "router").  Replaces the reference's t_attn / t_moe / t_head

@@ -7,12 +7,10 @@
 // one group splits every unit's K 12 ways (all warps busy on small
 // matrices); with many, up to 12 one-warp groups stream whole units (no
 // cross-warp reduction at all).  Per warp:
-//  * weights go straight from HBM into registers: per step (up to 4 T4 or 8
-//    T8 k-blocks of one unit) every lane loads its 16-byte A fragment of each
-//    block and its rows' group scales, one step ahead of the step it computes;
-//    HBM latency is covered by L2 prefetches (one bulk request per slice) of
-//    the warp's slices of its next units (up to ~288 KB per SM), which hold
-//    no registers or shared memory;
+//  * weights stream from HBM through a per-warp ring of shared-memory step
+//    slots filled with cp.async: per step (up to 4 T4 or 8 T8 k-blocks of one
+//    unit) every lane copies its 16-byte A fragment of each block and its
+//    rows' group scales, R - 1 steps ahead of the step it computes;
 //  * the MMAs are s8 x s8 -> s32 m16n8k32: a nibble n becomes the signed byte
 //    16 (n - 8) in one or two logic ops, INT8 weights need nothing;
 //  * the input rows are scaled by a power of two, rounded to 22-bit integers
@@ -40,7 +38,6 @@ namespace {
 
 constexpr int NCONS = GEMV_CONSUMERS;
 constexpr int NCT = NCONS * 32;
-constexpr int PREFETCH_BYTES = 288 * 1024;  // weight bytes per SM requested into L2 ahead of use (42 MB in all)
 
 constexpr int OFF_JP = 0;                                        // int[MAX_JOBS + 1]
 constexpr int OFF_TILES = 4224;                                  // const uint8_t *[MAX_JOBS]
@@ -98,6 +95,20 @@ __device__ __forceinline__ float swiglu(float gate, float up, float limit, float
     return __fmul_rn(__fmul_rn(__fadd_rn(up, 1.0f), gate), sg);
 }
 
+// Shift sh of an input row with max |x| = m: 22 - E where m = f 2^E, f in
+// [0.5, 1) (frexpf), at most 126; 0 for a zero or non-finite row.  The
+// exponent is read from the bits for normal m.
+__device__ __forceinline__ int row_shift(float m) {
+    if (!(m > 0.0f && m <= 3.4e38f)) return 0;
+    const uint32_t b = __float_as_uint(m);
+    int E;
+    if (b >= 0x00800000u) E = (int)(b >> 23) - 126;
+    else frexpf(m, &E);
+    return min(126, 22 - E);
+}
+// 2^e for -126 <= e <= 127 (exact, what ldexpf(1, e) returns)
+__device__ __forceinline__ float pow2i(int e) { return __int_as_float((e + 127) << 23); }
+
 // Builds the input-row (B) operand of the s8 MMAs for input rows
 // rows[0..n) in shared memory, once per job.  Row r is scaled by 2^sh, sh =
 // 22 - (exponent of its max |x|), rounded to an integer v (|v| <= 2^22, the
@@ -153,17 +164,11 @@ __device__ void fill_B(const GemvParams &p, const int *rows, int n, SMeta *meta,
         e[2 * 4 * CPB] = make_uint2(pack_s8x4(lo[0], lo[1], lo[2], lo[3]), pack_s8x4(lo[4], lo[5], lo[6], lo[7]));
         e[3 * 4 * CPB] = make_uint2(0u, 0u);
     };
-    auto scale_of = [&](int r) {  // 2^sh of row r from the per-warp maxima
+    auto scale_of = [&](int r) {  // sh of row r from the per-warp maxima
         float m = 0.0f;
 #pragma unroll
         for (int w = 0; w < NCONS; ++w) m = fmaxf(m, meta->part[w][r]);
-        int sh = 0;
-        if (m > 0.0f && m <= 3.4e38f) {
-            int E;
-            frexpf(m, &E);  // m < 2^E
-            sh = min(126, 22 - E);
-        }
-        return sh;
+        return row_shift(m);
     };
     constexpr int IPT = 4;  // items per thread for the one-pass form
     if (total <= IPT * NCT) {
@@ -192,16 +197,31 @@ __device__ void fill_B(const GemvParams &p, const int *rows, int n, SMeta *meta,
             if (lane == 0) meta->part[cw][r] = m;
         }
         named_bar_sync(1, NCT);
-        if (ctid < nrows) {
-            const int sh = scale_of(ctid);
-            meta->scale[mb][ctid] = ldexpf(1.0f, sh);
-            // removes 2^sh and, for INT4, the factor 16 of the s8 nibble values
-            meta->inv[mb][ctid] = ldexpf(1.0f, -sh - (CPB == 2 ? 4 : 0));
+        // every warp folds the NCONS per-warp maxima itself (lane w reads
+        // warp w's): no second barrier, one shift per row
+        int sh[2 * NT];
+#pragma unroll
+        for (int r = 0; r < 2 * NT; ++r) {
+            float m = lane < NCONS ? meta->part[lane][r] : 0.0f;
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+            sh[r] = row_shift(m);
         }
+#pragma unroll
+        for (int r = 0; r < 2 * NT; ++r)
+            if (ctid == r && r < nrows) {
+                meta->scale[mb][r] = pow2i(sh[r]);
+                // removes 2^sh and, for INT4, the factor 16 of the s8 nibble values
+                meta->inv[mb][r] = ldexpf(1.0f, -sh[r] - (CPB == 2 ? 4 : 0));
+            }
 #pragma unroll
         for (int q = 0; q < IPT; ++q) {
             const int idx = ctid + q * NCT;
-            if (idx < total) store_item(idx, v[q], rq[q] < nrows ? ldexpf(1.0f, scale_of(rq[q])) : 1.0f);
+            float sc = 1.0f;
+#pragma unroll
+            for (int r = 0; r < 2 * NT; ++r)
+                if (rq[q] == r && r < nrows) sc = pow2i(sh[r]);
+            if (idx < total) store_item(idx, v[q], sc);
         }
         named_bar_sync(1, NCT);
         return;
@@ -230,7 +250,7 @@ __device__ void fill_B(const GemvParams &p, const int *rows, int n, SMeta *meta,
     named_bar_sync(1, NCT);
     if (ctid < nrows) {
         const int sh = scale_of(ctid);
-        meta->scale[mb][ctid] = ldexpf(1.0f, sh);
+        meta->scale[mb][ctid] = pow2i(sh);
         meta->inv[mb][ctid] = ldexpf(1.0f, -sh - (CPB == 2 ? 4 : 0));
     }
     // pass 2: each thread rounds four items per round so their loads overlap
@@ -242,7 +262,7 @@ __device__ void fill_B(const GemvParams &p, const int *rows, int n, SMeta *meta,
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
             const int idx = base + q * NCT;
-            if (idx < total) store_item(idx, v[q], rq[q] < nrows ? ldexpf(1.0f, scale_of(rq[q])) : 1.0f);
+            if (idx < total) store_item(idx, v[q], rq[q] < nrows ? pow2i(scale_of(rq[q])) : 1.0f);
         }
     }
     named_bar_sync(1, NCT);
@@ -615,18 +635,12 @@ __device__ __forceinline__ void gemv_cta(const GemvParams &p, uint8_t *smem, int
     auto slice = [&](int u, int jj) {  // this warp's bytes of unit u
         return stiles[jj] + ((int64_t)(u - jp[jj]) * p.kblocks + kb0) * BB;
     };
-    // HBM latency is covered by L2 prefetches PD group units ahead (no
-    // registers or shared memory held); L2 latency by loading the next step
-    // into registers while this one is computed.
-    const int PD = max(1, min(ntot, PREFETCH_BYTES / NCONS / max(1, need * BB)));
-    int pf_u, pf_j;
-    first_from(j0, pf_u, pf_j);
-    auto prefetch_next = [&]() {  // one bulk request per slice (block bytes are multiples of 16)
-        if (pf_u < u1 && nbw > 0) {
-            if (lane == 0) bulk_prefetch_l2(slice(pf_u, pf_j), (uint32_t)(nbw * BB));
-            advance(pf_u, pf_j);
-        }
-    };
+    // HBM latency is covered by the warps' rings alone (R - 1 steps in flight
+    // per warp).  Measured in the decode step: L2 prefetches of the next units
+    // on top of them made every launch slower (their flood of requests
+    // delays the latency-critical loads after the dependency wait: the input
+    // row, the epilogue operands), the lm_head by 40 %.
+    //
     // This warp's ring of R step slots in shared memory, filled with
     // cp.async (16 bytes per lane per copy, no registers held while in flight):
     // step s lives in slot s % R; R - 1 steps are in flight behind the one
@@ -657,7 +671,6 @@ __device__ __forceinline__ void gemv_cta(const GemvParams &p, uint8_t *smem, int
         ++ld_seq;
     };
     // weights do not depend on earlier kernels: start streaming before waiting for them
-    for (int i = 0; i < PD; ++i) prefetch_next();
     for (int i = 0; i < R - 1; ++i) issue_step();
 
     // inputs and outputs do
@@ -751,7 +764,6 @@ __device__ __forceinline__ void gemv_cta(const GemvParams &p, uint8_t *smem, int
             }
         }
         for (int u = lo + gi; u < hi; u += G, ++n) {
-            prefetch_next();
 #pragma unroll
             for (int nt = 0; nt < NT; ++nt)
 #pragma unroll

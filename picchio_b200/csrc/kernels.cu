@@ -149,15 +149,45 @@ __global__ void __launch_bounds__(256) router_kernel(const RouterParams r) {
         const int e = blockIdx.x * 2 + (warp >> 2), q = warp & 3;
         const bool vec = (r.D & 3) == 0;
         const int m1 = min(r.M, (int)(blockIdx.y + 1) * ROUTER_ROWS);
+        const bool fused = r.ln_w != nullptr;
         for (int m = blockIdx.y * ROUTER_ROWS; m < m1; ++m) {
+            float rn = 1.0f;
+            if (fused) {  // the input norm of this row, as rmsnorm_kernel computes it
+                const int n4 = r.D >> 2;
+                const float4 *h4 = reinterpret_cast<const float4 *>(r.h_in + (int64_t)m * r.D);
+                const float4 *w4 = reinterpret_cast<const float4 *>(r.ln_w);
+                float4 hv[NORM_V4];
+                double ss = 0.0;
+#pragma unroll
+                for (int j = 0; j < NORM_V4; ++j) {
+                    const int i = threadIdx.x + j * NORM_THREADS;
+                    hv[j] = i < n4 ? h4[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+                    ss += (double)hv[j].x * hv[j].x + (double)hv[j].y * hv[j].y + (double)hv[j].z * hv[j].z +
+                          (double)hv[j].w * hv[j].w;
+                }
+                rn = norm_scale(ss, r.D, r.eps);
+                if (blockIdx.x == 0) {
+                    float4 *o4 = reinterpret_cast<float4 *>(r.hn_out + (int64_t)m * r.D);
+#pragma unroll
+                    for (int j = 0; j < NORM_V4; ++j) {
+                        const int i = threadIdx.x + j * NORM_THREADS;
+                        if (i < n4) {
+                            const float4 w = w4[i];
+                            o4[i] = make_float4(__fmul_rn(__fmul_rn(hv[j].x, rn), w.x), __fmul_rn(__fmul_rn(hv[j].y, rn), w.y),
+                                                __fmul_rn(__fmul_rn(hv[j].z, rn), w.z), __fmul_rn(__fmul_rn(hv[j].w, rn), w.w));
+                        }
+                    }
+                }
+            }
             float s = 0.0f;
             if (e < r.E) {
                 const float *re = r.R + (int64_t)e * r.D;
-                const float *xr = r.x + (int64_t)m * r.D;
+                const float *xr = fused ? r.h_in + (int64_t)m * r.D : r.x + (int64_t)m * r.D;
                 if (vec) {
                     const int n4 = r.D >> 2, i0 = n4 * q / 4, i1 = n4 * (q + 1) / 4;
                     const float4 *r4 = reinterpret_cast<const float4 *>(re);
                     const float4 *x4 = reinterpret_cast<const float4 *>(xr);
+                    const float4 *w4 = reinterpret_cast<const float4 *>(r.ln_w);
                     float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
                     for (int base = i0 + lane; base < i1; base += 32 * ROUTER_RV) {
                         float4 rv[ROUTER_RV], xv[ROUTER_RV];
@@ -166,6 +196,17 @@ __global__ void __launch_bounds__(256) router_kernel(const RouterParams r) {
                             const int i = base + 32 * j;
                             rv[j] = i < i1 ? r4[i] : make_float4(0.f, 0.f, 0.f, 0.f);
                             xv[j] = i < i1 ? x4[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+                        }
+                        if (fused) {
+#pragma unroll
+                            for (int j = 0; j < ROUTER_RV; ++j) {
+                                const int i = base + 32 * j;
+                                const float4 w = i < i1 ? w4[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+                                xv[j] = make_float4(__fmul_rn(__fmul_rn(xv[j].x, rn), w.x),
+                                                    __fmul_rn(__fmul_rn(xv[j].y, rn), w.y),
+                                                    __fmul_rn(__fmul_rn(xv[j].z, rn), w.z),
+                                                    __fmul_rn(__fmul_rn(xv[j].w, rn), w.w));
+                            }
                         }
 #pragma unroll
                         for (int j = 0; j < ROUTER_RV; ++j) {
@@ -535,6 +576,7 @@ cudaError_t launch_rmsnorm(const float *x, const float *w, float *out, int M, in
 
 cudaError_t launch_router(const RouterParams &r, cudaStream_t st) {
     if (r.E > 256 || r.K > 16 || r.M * r.K > GEMV_MAX_JOBS) return cudaErrorInvalidValue;
+    if (r.ln_w && ((r.D & 3) || r.D > 4 * NORM_V4 * NORM_THREADS || !r.h_in || !r.hn_out)) return cudaErrorInvalidValue;
     const dim3 grid = r.sel_in ? dim3(1) : dim3((r.E + 1) / 2, (r.M + ROUTER_ROWS - 1) / ROUTER_ROWS);
     return launch_k(router_kernel, grid, dim3(256), 0, st, r);
     return cudaGetLastError();

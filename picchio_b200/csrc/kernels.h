@@ -49,6 +49,12 @@ struct RouterParams {
     float *w;              // [M][K]
     unsigned *counter;     // zero, self-resetting
     const int *sel_in;     // optional given routing [M][K] (skips router + top-k)
+    // optional fused input norm: x[m] = rmsnorm(h_in[m], ln_w, eps) computed
+    // in every block (exactly as rmsnorm_kernel does), written to hn_out[m]
+    // by the blocks with blockIdx.x == 0; r.x is then unused.  D % 4 == 0.
+    const float *h_in, *ln_w;
+    float eps;
+    float *hn_out;
     const float *w_in;
     // job building for the expert GEMVs
     const uint8_t *table;  // this layer's expert table

@@ -80,15 +80,20 @@ struct Prof {
     pc_ctx *c;
     const char *label;
     cudaEvent_t a = nullptr, b = nullptr;
+    unsigned flags = 0;
     Prof(pc_ctx *cc, const char *l) : c(cc), label(l) {
         if (!c->prof) return;
         cudaEventCreate(&a);
         cudaEventCreate(&b);
-        cudaEventRecord(a, c->st);
+        // under stream capture the record must be an (external) graph node
+        cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+        cudaStreamIsCapturing(c->st, &cs);
+        flags = cs == cudaStreamCaptureStatusActive ? cudaEventRecordExternal : cudaEventRecordDefault;
+        cudaEventRecordWithFlags(a, c->st, flags);
     }
     ~Prof() {
         if (!a) return;
-        cudaEventRecord(b, c->st);
+        cudaEventRecordWithFlags(b, c->st, flags);
         c->prof_evs.push_back({label, a, b});
     }
 };
@@ -294,8 +299,12 @@ void trace_row_i(pc_ctx *c, const std::string &name, const int *dev, int n) {
 // router (or given routing), gate_up + SwiGLU, down, combine.
 // With next_ln set, the combine also writes c->hn = rmsnorm(h, next_ln): the
 // next layer's input norm or the final norm, saving their launches.
+// With norm_ln set, x is rmsnorm(h, norm_ln), computed inside the router
+// kernel (which also writes it to x, i.e. c->hn) instead of by a launch of
+// its own.
 pc_status run_moe(pc_ctx *c, int l, const float *x, int M, const int *sel_in, const float *w_in,
-                  int bias_first, float *out, float *h, const float *next_ln = nullptr) {
+                  int bias_first, float *out, float *h, const float *next_ln = nullptr,
+                  const float *norm_ln = nullptr) {
     const pc_model_cfg &k = c->cfg;
     const int K = k.topk, D = k.hidden;
     Layer &ly = c->L[l];
@@ -339,6 +348,12 @@ pc_status run_moe(pc_ctx *c, int l, const float *x, int M, const int *sel_in, co
     r.per_job = (M > GEMV_MAXR && (int64_t)M * K <= 3LL * k.n_experts) ? 4 : GEMV_MAXR;
     r.njobs = c->njobs;
     r.pair_local = c->pair_local;
+    if (norm_ln) {
+        r.h_in = h;
+        r.ln_w = norm_ln;
+        r.eps = k.eps;
+        r.hn_out = const_cast<float *>(x);
+    }
     {
         Prof pr(c, "router");
         PC_CU(launch_router(r, c->st));
@@ -510,11 +525,17 @@ pc_status run_step(pc_ctx *c, int M, const int *seq, int lm_mode, int nsplit_ful
             cudaMemcpy(c->h, hh.data(), hh.size() * 4, cudaMemcpyHostToDevice);
         }
         trace_row(c, pre + "post_attn_residual", c->h + (size_t)last * D, D);
-        PC_CU(launch_rmsnorm(c->h, ly.post_ln, c->hn, M, D, k.eps, c->st));
-        ++c->launches;
+        // the post-attention norm runs inside the router kernel, except when
+        // tracing (its output is recorded before the router runs)
+        const bool fuse_norm = !c->trace && (D & 3) == 0 && D <= 4096;
+        if (!fuse_norm) {
+            PC_CU(launch_rmsnorm(c->h, ly.post_ln, c->hn, M, D, k.eps, c->st));
+            ++c->launches;
+        }
         trace_row(c, pre + "pre_moe_norm", c->hn + (size_t)last * D, D);
         const float *next_ln = l + 1 < k.n_layers ? c->L[l + 1].in_ln : c->final_norm;
-        PC_TRY(run_moe(c, l, c->hn, M, nullptr, nullptr, 0, c->trace ? c->moe_out : nullptr, c->h, next_ln));
+        PC_TRY(run_moe(c, l, c->hn, M, nullptr, nullptr, 0, c->trace ? c->moe_out : nullptr, c->h, next_ln,
+                       fuse_norm ? ly.post_ln : nullptr));
         trace_row(c, pre + "moe_out", c->moe_out + (size_t)last * D, D);
         trace_row(c, pre + "output", c->h + (size_t)last * D, D);
     }
@@ -581,6 +602,25 @@ pc_status check_err(pc_ctx *c) {
 // or profiled (those need host work between kernels).
 template <typename F>
 pc_status run_graph(pc_ctx *c, uint64_t key, F &&body) {
+    if (c->prof && c->opts.use_graphs && !c->trace) {
+        // profiled step: a one-off graph, so that the events around each
+        // launch (graph nodes) time the device without host launch gaps
+        cudaGraph_t g = nullptr;
+        PC_CU(cudaStreamBeginCapture(c->st, cudaStreamCaptureModeThreadLocal));
+        pc_status s = body();
+        cudaError_t e = cudaStreamEndCapture(c->st, &g);
+        if (s != PC_OK) { if (g) cudaGraphDestroy(g); return s; }
+        if (e != cudaSuccess) return cuda_fail(e, "cudaStreamEndCapture");
+        cudaGraphExec_t ex = nullptr;
+        e = cudaGraphInstantiate(&ex, g, 0);
+        cudaGraphDestroy(g);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaGraphInstantiate");
+        e = cudaGraphLaunch(ex, c->st);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(c->st);
+        cudaGraphExecDestroy(ex);
+        if (e != cudaSuccess) return cuda_fail(e, "profiled step");
+        return PC_OK;
+    }
     if (!c->opts.use_graphs || c->trace || c->prof) return body();
     auto it = c->graphs.find(key);
     if (it == c->graphs.end()) {
