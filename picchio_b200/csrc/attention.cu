@@ -9,10 +9,9 @@ namespace {
 
 template <typename T, int HD>
 __global__ void __launch_bounds__(NT) attn_kernel(const AttnParams a) {
-    pdl_wait();
     pdl_trigger();
     __shared__ AttnSmem<HD> sm;
-    attn_item<T, HD>(a, blockIdx.x, blockIdx.y, blockIdx.z, sm, 0);
+    attn_item<T, HD, true>(a, blockIdx.x, blockIdx.y, blockIdx.z, sm, 0);  // waits inside
 }
 
 template <typename T>

@@ -14,11 +14,12 @@
 //    position groups are then summed in a fixed order.
 // The last item of a (row, KV head) to finish (atomic ticket) merges the
 // spans with the sink, which joins the max and the denominator only
-// (picchio.c:586-596).
+// (picchio.c:586-596); a row whose positions fit one span merges in place.
 #pragma once
 #include <cuda_bf16.h>
 
 #include "kernels.h"
+#include "launch.cuh"
 #include "ptx.cuh"
 
 namespace pc {
@@ -37,21 +38,37 @@ __device__ __forceinline__ float4 load4(const __nv_bfloat16 *p) {
     return make_float4(x.x, x.y, y.x, y.y);
 }
 
+// A K row's 4 elements as loaded (no conversion, so the load does not block)
+__device__ __forceinline__ float4 load4_raw(const float *p) { return *reinterpret_cast<const float4 *>(p); }
+__device__ __forceinline__ uint2 load4_raw(const __nv_bfloat16 *p) { return *reinterpret_cast<const uint2 *>(p); }
+__device__ __forceinline__ float4 raw_to_f4(float4 v) { return v; }
+__device__ __forceinline__ float4 raw_to_f4(uint2 a) {
+    const float2 x = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&a.x));
+    const float2 y = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&a.y));
+    return make_float4(x.x, x.y, y.x, y.y);
+}
+template <typename T> struct Raw4 { using type = float4; };
+template <> struct Raw4<__nv_bfloat16> { using type = uint2; };
+
 // Shared memory of one work item.
 template <int HD>
-struct AttnSmem {
+struct alignas(16) AttnSmem {
     float qs[MAXG][HD];
     float ps[MAXG][NT];
     float wred[MAXG][NT / 32];
     float mloc[MAXG], lloc[MAXG];
     float ored[NT / 32][MAXG][HD];
     float mrec[MAXG][64], lrec[MAXG][64];
+    float lsum[MAXG];
     bool last;
 };
 
 // One work item: span s of KV head kh of row m, run by NT threads (t =
-// threadIdx.x < NT) that synchronize on named barrier `bar`.
-template <typename T, int HD>
+// threadIdx.x < NT) that synchronize on named barrier `bar`.  PDL: the item
+// runs in a programmatic dependent launch: for a single row, the K rows of
+// earlier positions (written by earlier steps) are requested before waiting
+// for the kernel that writes this step's q and K/V row.
+template <typename T, int HD, bool PDL = false>
 __device__ __forceinline__ void attn_item(const AttnParams &a, int s, int kh, int m, AttnSmem<HD> &sm, int bar) {
     auto &qs = sm.qs;
     auto &ps = sm.ps;
@@ -73,6 +90,10 @@ __device__ __forceinline__ void attn_item(const AttnParams &a, int s, int kh, in
         start = end - a.window + 1;
         if (start < 0) start = 0;
     }
+    // spans that hold positions; a launch may have more (a power-of-two
+    // bucket shared by nearby positions), which leave at once
+    const int nsp = (end - start + NT) / NT;
+    if (s >= nsp) return;
     const int p0 = start + s * NT;
     const int cnt = max(0, min(NT, end + 1 - p0));
     const int64_t cache0 = (int64_t)a.row_seq[m] * a.seq_stride + kh * HD;
@@ -80,14 +101,21 @@ __device__ __forceinline__ void attn_item(const AttnParams &a, int s, int kh, in
     // The KV rows of the span do not depend on q: this thread's K row goes
     // into registers and its V row into L2 before q is even loaded, so the
     // cache's HBM latency is paid once, overlapped with q and the scores.
-    float4 k4[HD / 4];
-    if (t < cnt) {
+    typename Raw4<T>::type k4[HD / 4];
+    auto load_kv = [&]() {
         const T *kr = Kc + cache0 + (int64_t)(p0 + t) * kvd;
 #pragma unroll
-        for (int i = 0; i < HD / 4; ++i) k4[i] = load4(kr + 4 * i);
+        for (int i = 0; i < HD / 4; ++i) k4[i] = load4_raw(kr + 4 * i);
         const char *vr = reinterpret_cast<const char *>(Vc + cache0 + (int64_t)(p0 + t) * kvd);
         for (int o = 0; o < (int)(HD * sizeof(T)); o += 128) prefetch_l2(vr + o);
-    }
+    };
+    // Rows of this step write K/V at their own positions: with one row that is
+    // only position pos; with several (a prefill chunk shares one sequence)
+    // every load waits.
+    const bool fresh = a.M > 1 || p0 + t == pos;
+    if (t < cnt && !fresh) load_kv();
+    if (PDL) pdl_wait();
+    if (t < cnt && fresh) load_kv();
     for (int i = t; i < G * HD; i += NT) qs[i / HD][i % HD] = a.q[(int64_t)m * a.H * HD + (kh * G) * HD + i];
     named_bar_sync(bar, NT);
     const float scale = __fdiv_rn(1.0f, sqrtf((float)HD));
@@ -95,14 +123,20 @@ __device__ __forceinline__ void attn_item(const AttnParams &a, int s, int kh, in
         float dot[MAXG];
 #pragma unroll
         for (int g = 0; g < MAXG; ++g) dot[g] = 0.0f;
+        // per head the sequential order of the reference (i = 0..hd-1); q is
+        // read from shared memory 4 elements at a time
 #pragma unroll
         for (int i = 0; i < HD / 4; ++i) {
-            const float kv[4] = {k4[i].x, k4[i].y, k4[i].z, k4[i].w};
+            const float4 kv = raw_to_f4(k4[i]);
 #pragma unroll
-            for (int j = 0; j < 4; ++j)
-#pragma unroll
-                for (int g = 0; g < MAXG; ++g)
-                    if (g < G) dot[g] = __fadd_rn(dot[g], __fmul_rn(qs[g][4 * i + j], kv[j]));
+            for (int g = 0; g < MAXG; ++g)
+                if (g < G) {
+                    const float4 qv = *reinterpret_cast<const float4 *>(&qs[g][4 * i]);
+                    dot[g] = __fadd_rn(dot[g], __fmul_rn(qv.x, kv.x));
+                    dot[g] = __fadd_rn(dot[g], __fmul_rn(qv.y, kv.y));
+                    dot[g] = __fadd_rn(dot[g], __fmul_rn(qv.z, kv.z));
+                    dot[g] = __fadd_rn(dot[g], __fmul_rn(qv.w, kv.w));
+                }
         }
 #pragma unroll
         for (int g = 0; g < MAXG; ++g)
@@ -186,6 +220,28 @@ __device__ __forceinline__ void attn_item(const AttnParams &a, int s, int kh, in
         }
     }
     named_bar_sync(bar, NT);
+    if (nsp == 1) {
+        // one span: the merge below for a single span, in the same arithmetic
+        // (so results equal the multi-span path's), without the round trip
+        // through the partial records
+        for (int idx = t; idx < G * HD; idx += NT) {
+            const int g = idx / HD, d = idx % HD, h = kh * G + g;
+            float o = 0.0f;
+#pragma unroll
+            for (int w = 0; w < NT / 32; ++w) o = __fadd_rn(o, ored[w][g][d]);
+            float M = a.sinks ? a.sinks[h] : -INFINITY;
+            M = fmaxf(M, mloc[g]);
+            float L = a.sinks ? expf(__fsub_rn(a.sinks[h], M)) : 0.0f;
+            float O = 0.0f;
+            if (lloc[g] != 0.0f) {
+                const float f = expf(__fsub_rn(mloc[g], M));
+                L = __fmaf_rn(lloc[g], f, L);
+                O = __fmaf_rn(o, f, O);
+            }
+            a.out[(int64_t)m * a.H * HD + h * HD + d] = __fdiv_rn(O, L);
+        }
+        return;
+    }
     const int stride = HD + 2;
     for (int idx = t; idx < G * HD; idx += NT) {
         const int g = idx / HD, d = idx % HD;
@@ -203,15 +259,15 @@ __device__ __forceinline__ void attn_item(const AttnParams &a, int s, int kh, in
     named_bar_sync(bar, NT);
     if (t == 0) {
         unsigned *c = a.counter + m * a.KVH + kh;
-        last = atomicAdd(c, 1u) == (unsigned)(a.nsplit - 1);
+        last = atomicAdd(c, 1u) == (unsigned)(nsp - 1);
         if (last) *c = 0u;
     }
     named_bar_sync(bar, NT);
     if (!last) return;
     __threadfence();
     // merge the spans: (m, l) of every span into shared memory first
-    for (int idx = t; idx < G * a.nsplit; idx += NT) {
-        const int g = idx / a.nsplit, k = idx % a.nsplit;
+    for (int idx = t; idx < G * nsp; idx += NT) {
+        const int g = idx / nsp, k = idx % nsp;
         const float *rec = a.part + (((int64_t)m * a.H + kh * G + g) * a.nsplit + k) * stride;
         if (k < 64) {
             mrec[g][k] = __ldcg(rec);
@@ -219,27 +275,40 @@ __device__ __forceinline__ void attn_item(const AttnParams &a, int s, int kh, in
         }
     }
     named_bar_sync(bar, NT);
+    // per head, once: the max M over the sink and the spans, the span weights
+    // f_k = exp(m_k - M) (in place of m_k) and the denominator
+    if (t < G) {
+        const int g = t, h = kh * G + g;
+        float M = a.sinks ? a.sinks[h] : -INFINITY;
+        for (int k = 0; k < nsp; ++k) M = fmaxf(M, mrec[g][k]);
+        float L = a.sinks ? expf(__fsub_rn(a.sinks[h], M)) : 0.0f;
+        for (int k = 0; k < nsp; ++k) {
+            float f = 0.0f;
+            if (lrec[g][k] != 0.0f) {
+                f = expf(__fsub_rn(mrec[g][k], M));
+                L = __fmaf_rn(lrec[g][k], f, L);
+            }
+            mrec[g][k] = f;
+        }
+        sm.lsum[g] = L;
+    }
+    named_bar_sync(bar, NT);
     for (int idx = t; idx < G * HD; idx += NT) {
         const int g = idx / HD, d = idx % HD, h = kh * G + g;
         const float *rec0 = a.part + (((int64_t)m * a.H + h) * a.nsplit) * stride;
-        float M = a.sinks ? a.sinks[h] : -INFINITY;
-        for (int k = 0; k < a.nsplit; ++k) M = fmaxf(M, mrec[g][k]);
-        float L = a.sinks ? expf(__fsub_rn(a.sinks[h], M)) : 0.0f;
         float O = 0.0f;
-        for (int k0 = 0; k0 < a.nsplit; k0 += 8) {
-            float ov[8];
+        for (int k0 = 0; k0 < nsp; k0 += 16) {
+            float ov[16];
 #pragma unroll
-            for (int j = 0; j < 8; ++j) ov[j] = k0 + j < a.nsplit ? __ldcg(rec0 + (k0 + j) * stride + 2 + d) : 0.0f;
+            for (int j = 0; j < 16; ++j) ov[j] = k0 + j < nsp ? __ldcg(rec0 + (k0 + j) * stride + 2 + d) : 0.0f;
 #pragma unroll
-            for (int j = 0; j < 8; ++j) {
+            for (int j = 0; j < 16; ++j) {
                 const int k = k0 + j;
-                if (k >= a.nsplit || lrec[g][k] == 0.0f) continue;
-                const float f = expf(__fsub_rn(mrec[g][k], M));
-                L = __fmaf_rn(lrec[g][k], f, L);
-                O = __fmaf_rn(ov[j], f, O);
+                if (k >= nsp || lrec[g][k] == 0.0f) continue;
+                O = __fmaf_rn(ov[j], mrec[g][k], O);
             }
         }
-        a.out[(int64_t)m * a.H * HD + h * HD + d] = __fdiv_rn(O, L);
+        a.out[(int64_t)m * a.H * HD + h * HD + d] = __fdiv_rn(O, sm.lsum[g]);
     }
 }
 

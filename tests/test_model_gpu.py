@@ -255,3 +255,29 @@ def test_tensor_core_split_k_prefill_matches_sequential():
             t2 = b.forward_token(t, i)
         assert t1 == t2
         assert rel_l2(a.logits(0), b.logits(0)) < 1e-5
+
+
+def test_long_context_multi_span_attention_matches_oracle():
+    """600 positions: full-attention layers split each (row, KV head) over
+    3 spans of 256 positions and merge them (the 128-position sliding window
+    stays in one span).  A 600-token prefill, then 3 decode steps, against
+    the oracle's sequential forward_token over the same ids."""
+    from picchio_b200 import Model
+    m = meta("tiny_gs32_i8")
+    import tempfile
+    d = tempfile.mkdtemp()
+    make_model(d, SynthConfig(**m["options"]), m["seed"])
+    n, steps = 600, 3
+    ids = [int(v) for v in np.random.default_rng(9).integers(0, 1024, n)]
+    orc = O.OracleModel(d, ctx=n + 8)
+    ref_tok, ref_logits = None, None
+    for i, t in enumerate(ids):
+        ref_tok, ref_logits = orc.forward_token(t, i, return_logits=True)
+    with Model(d, ctx=n + 8) as model:
+        tok = model.prefill_tokens(ids, 0)
+        assert tok == ref_tok
+        assert rel_l2(model.logits(0), ref_logits) < 1e-4
+        for s in range(steps):
+            ref_tok = orc.forward_token(ref_tok, n + s)
+            tok = model.forward_token(tok, n + s)
+            assert tok == ref_tok, s
