@@ -118,6 +118,10 @@ struct pc_ctx {
     // dense weights as row-major copies (per layer q, k, v, o; then lm_head)
     pc::TcState tc;
     std::vector<pc::TcWeight> tcw;
+    // expert GEMMs on the tensor cores (tcgemm.cu): gathered f16 rows and the
+    // router's expert-sorted pair lists
+    pc::TcExpState tex;
+    int *pair_start = nullptr, *pair_list = nullptr;
 
     // persistent decode kernel (decode.cu): 0 = not set up yet, 1 = used, -1 = not applicable
     int dec_state = 0;

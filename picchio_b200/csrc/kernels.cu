@@ -141,8 +141,8 @@ __global__ void __launch_bounds__(256) router_kernel(const RouterParams r) {
     pdl_trigger();
     __shared__ bool last;
     __shared__ float part[8];
-    __shared__ int cnt[256], jstart[257];
-    __shared__ int ssel[GEMV_MAX_JOBS];
+    __shared__ int cnt[256], jstart[257], pstart[257];
+    __shared__ int ssel[ROUTER_MAX_PAIRS];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int P = r.M * r.K;
     if (!r.sel_in) {
@@ -284,7 +284,7 @@ __global__ void __launch_bounds__(256) router_kernel(const RouterParams r) {
                 for (int k = 0; k < r.K; ++k) { wk[k] = expf(__fsub_rn(wk[k], mx)); sum = __fadd_rn(sum, wk[k]); }
                 for (int k = 0; k < r.K; ++k) {
                     r.sel[m * r.K + k] = sk[k];
-                    if (m * r.K + k < GEMV_MAX_JOBS) ssel[m * r.K + k] = sk[k];
+                    if (m * r.K + k < ROUTER_MAX_PAIRS) ssel[m * r.K + k] = sk[k];
                     r.w[m * r.K + k] = __fdiv_rn(wk[k], sum);
                 }
             }
@@ -295,13 +295,13 @@ __global__ void __launch_bounds__(256) router_kernel(const RouterParams r) {
         for (int i = threadIdx.x; i < P; i += blockDim.x) {
             const int v = r.sel_in[i];
             r.sel[i] = v;
-            if (i < GEMV_MAX_JOBS) ssel[i] = v;
+            if (i < ROUTER_MAX_PAIRS) ssel[i] = v;
             r.w[i] = r.w_in[i];
         }
         __syncthreads();
     }
     // expert job tables: pairs grouped by expert, at most pj pairs per job
-    const int Ps = min(P, GEMV_MAX_JOBS);
+    const int Ps = min(P, ROUTER_MAX_PAIRS);
     const int pj = (r.per_job > 0 && r.per_job < GEMV_MAXR) ? r.per_job : GEMV_MAXR;
     const int e = threadIdx.x;
     int n = 0;
@@ -309,7 +309,24 @@ __global__ void __launch_bounds__(256) router_kernel(const RouterParams r) {
         for (int p = 0; p < Ps; ++p) n += (ssel[p] == e);
     }
     cnt[e] = (n + pj - 1) / pj;
+    pstart[e] = n;
     __syncthreads();
+    if (r.pair_start && warp == 1) {  // exclusive scan of pairs per expert
+        int v[8], tot = 0;
+#pragma unroll
+        for (int q = 0; q < 8; ++q) { v[q] = tot; tot += pstart[lane * 8 + q]; }
+        int inc = tot;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int nn = __shfl_up_sync(0xffffffffu, inc, o);
+            if (lane >= o) inc += nn;
+        }
+        const int base = inc - tot;
+        __syncwarp();
+#pragma unroll
+        for (int q = 0; q < 8; ++q) pstart[lane * 8 + q] = base + v[q];
+        if (lane == 31) pstart[256] = inc;
+    }
     if (warp == 0) {  // exclusive scan of jobs per expert: 8 experts per lane
         int v[8], tot = 0;
 #pragma unroll
@@ -332,6 +349,15 @@ __global__ void __launch_bounds__(256) router_kernel(const RouterParams r) {
     for (int p = threadIdx.x; p < Ps; p += blockDim.x) {
         const int ep = ssel[p];
         r.pair_local[p] = (ep >= r.e_lo && ep < r.e_hi) ? 1 : 0;
+    }
+    if (r.pair_start) {
+        if (e < r.E) r.pair_start[e] = pstart[e];
+        if (e == 0) r.pair_start[r.E] = pstart[256];
+        if (n > 0) {
+            int q = pstart[e];
+            for (int p = 0; p < Ps; ++p)
+                if (ssel[p] == e) r.pair_list[q++] = p;
+        }
     }
     if (n == 0) return;
     const int slot = r.slot_of ? r.slot_of[e] : e - r.e_lo;
@@ -575,7 +601,10 @@ cudaError_t launch_rmsnorm(const float *x, const float *w, float *out, int M, in
 
 
 cudaError_t launch_router(const RouterParams &r, cudaStream_t st) {
-    if (r.E > 256 || r.K > 16 || r.M * r.K > GEMV_MAX_JOBS) return cudaErrorInvalidValue;
+    // more pairs than one job table holds only with the expert-sorted pair
+    // lists (the tensor-core expert path reads those, not the jobs)
+    if (r.E > 256 || r.K > 16 || r.M * r.K > (r.pair_start ? ROUTER_MAX_PAIRS : GEMV_MAX_JOBS))
+        return cudaErrorInvalidValue;
     if (r.ln_w && ((r.D & 3) || r.D > 4 * NORM_V4 * NORM_THREADS || !r.h_in || !r.hn_out)) return cudaErrorInvalidValue;
     const dim3 grid = r.sel_in ? dim3(1) : dim3((r.E + 1) / 2, (r.M + ROUTER_ROWS - 1) / ROUTER_ROWS);
     return launch_k(router_kernel, grid, dim3(256), 0, st, r);

@@ -38,6 +38,8 @@ constexpr int ATTN_SPLIT = 256;
 // gqa_attention's score / softmax-with-sink / P.V part (picchio.c:556-607).
 cudaError_t launch_attention(const AttnParams &a, cudaStream_t st);
 
+constexpr int ROUTER_MAX_PAIRS = 4096;  // (row, k) pairs one router launch sorts by expert
+
 struct RouterParams {
     const float *x;        // [M][D] normalized rows
     const float *R;        // [E][D]
@@ -67,6 +69,10 @@ struct RouterParams {
     int per_job;           // (row, k) pairs per job, 1..GEMV_MAXR (0 = GEMV_MAXR)
     int *njobs;            // [2]: gate_up, down
     int *pair_local;       // [M*K] 1 if the pair's expert is resident here
+    // optional: pairs sorted by expert (pair_list, ascending pair index within
+    // an expert) and each expert's first entry (pair_start[E + 1]); resident
+    // experts only
+    int *pair_start, *pair_list;
 };
 // Router dot products (picchio.c:1316-1324), top-k with strict '>'
 // (picchio.c:1330-1340), softmax over the k logits (picchio.c:1355), and the

@@ -299,6 +299,63 @@ void trace_row_i(pc_ctx *c, const std::string &name, const int *dev, int n) {
 // router (or given routing), gate_up + SwiGLU, down, combine.
 // With next_ln set, the combine also writes c->hn = rmsnorm(h, next_ln): the
 // next layer's input norm or the final norm, saving their launches.
+// The expert half of run_moe on the tensor cores (after the router kernel
+// wrote the expert-sorted pair lists): gate_up + SwiGLU, down, combine.
+pc_status run_moe_tc(pc_ctx *c, int l, const float *x, int M, float *out, float *h, const float *next_ln) {
+    const pc_model_cfg &k = c->cfg;
+    const int K = k.topk, D = k.hidden, P = M * K;
+    Layer &ly = c->L[l];
+    const bool ep = c->nccl_comm != nullptr;
+    TcExpParams t;
+    memset(&t, 0, sizeof t);
+    t.table = ly.experts;
+    t.stride = c->eg.stride;
+    t.e_lo = c->e_lo;
+    t.e_hi = c->e_hi;
+    t.pair_start = c->pair_start;
+    t.pair_list = c->pair_list;
+    t.bmap = c->tex.bmap;
+    t.err = c->err;
+    auto geom = [&](const TileDesc &g, int64_t off, int64_t off_rs, int64_t off_b) {
+        t.off_tiles = off;
+        t.off_rs = off_rs;
+        t.off_bias = off_b;
+        t.kblocks = g.kblocks;
+        t.blk_bytes = g.blk_bytes;
+        t.n_rt = g.Op / 16;
+        t.O = g.O;
+        t.Ip = g.Ip;
+        t.perm = g.perm;
+    };
+    {
+        Prof pr(c, "expert_gate_up");
+        PC_CU(tc_exp_gather(c->tex, x, D, D, K, false, c->pair_start, c->pair_list, k.n_experts, P, c->st));
+        geom(c->eg.gu, c->eg.off_gu, c->eg.off_gu_rs, c->eg.off_gu_b);
+        t.epi = EPI_SWIGLU;
+        t.y = c->act;
+        t.ldy = k.intermediate;
+        t.swiglu_limit = k.swiglu_limit;
+        t.swiglu_alpha = k.swiglu_alpha;
+        PC_CU(tc_exp_launch(t, c->eg.gu.gs, c->e_hi - c->e_lo, P, c->st));
+    }
+    if (ep) PC_CU(cudaMemsetAsync(c->eo, 0, (size_t)P * D * 4, c->st));
+    {
+        Prof pr(c, "expert_down");
+        PC_CU(tc_exp_gather(c->tex, c->act, k.intermediate, k.intermediate, K, true, c->pair_start, c->pair_list,
+                            k.n_experts, P, c->st));
+        geom(c->eg.dn, c->eg.off_dn, c->eg.off_dn_rs, c->eg.off_dn_b);
+        t.epi = EPI_STORE;
+        t.y = c->eo;
+        t.ldy = D;
+        PC_CU(tc_exp_launch(t, c->eg.dn.gs, c->e_hi - c->e_lo, P, c->st));
+    }
+    c->launches += 4;
+    if (ep) PC_TRY(ep_allreduce_sum(c, c->eo, (size_t)P * D));
+    PC_CU(launch_combine(c->eo, c->rw, c->sel, k.routed_scale, M, K, D, out, h, c->st, next_ln, k.eps, c->hn));
+    ++c->launches;
+    return PC_OK;
+}
+
 // With norm_ln set, x is rmsnorm(h, norm_ln), computed inside the router
 // kernel (which also writes it to x, i.e. c->hn) instead of by a launch of
 // its own.
@@ -348,6 +405,14 @@ pc_status run_moe(pc_ctx *c, int l, const float *x, int M, const int *sel_in, co
     r.per_job = (M > GEMV_MAXR && (int64_t)M * K <= 3LL * k.n_experts) ? 4 : GEMV_MAXR;
     r.njobs = c->njobs;
     r.pair_local = c->pair_local;
+    // many pairs per expert (large prefill chunks, the single-layer
+    // microbench): expert GEMMs on the tensor cores, fed by the router's
+    // expert-sorted pair lists
+    const bool tc_exp = c->tex.on && !c->trace && (int64_t)M * K >= (int64_t)TE_MIN_PAIRS * k.n_experts;
+    if (tc_exp) {
+        r.pair_start = c->pair_start;
+        r.pair_list = c->pair_list;
+    }
     if (norm_ln) {
         r.h_in = h;
         r.ln_w = norm_ln;
@@ -365,6 +430,7 @@ pc_status run_moe(pc_ctx *c, int l, const float *x, int M, const int *sel_in, co
         trace_row_i(c, "layer" + std::to_string(l) + ".top_indices", c->sel + (size_t)last * K, K);
         trace_row(c, "layer" + std::to_string(l) + ".top_weights", c->rw + (size_t)last * K, K);
     }
+    if (tc_exp) return run_moe_tc(c, l, x, M, out, h, next_ln);
     const int rows = std::min(M, r.per_job);
     GemvParams p{};
     params_for(p, c->eg.gu, EPI_SWIGLU);
@@ -880,13 +946,25 @@ pc_status make_ctx(const pc_opts *opts, pc_ctx **out) {
     return PC_OK;
 }
 
-// The tensor-core path for batches of 16..128 rows (tcgemm.cu): row-major
-// copies of every INT8 dense projection and the shared digit / partial-sum
-// buffers.  Off when a dense projection is not INT8, when the driver's
-// tensor-map encoder is unavailable, or with PICCHIO_TC=0.
+// The tensor-core paths (tcgemm.cu): for INT4 experts, the gathered-row
+// buffer and pair lists of the expert GEMMs; for INT8 dense projections,
+// their row-major copies and the shared digit / partial-sum buffers (batches
+// of 16..128 rows).  Off without the driver's tensor-map encoder or with
+// PICCHIO_TC=0.
 pc_status tc_setup(pc_ctx *c) {
     const char *v = getenv("PICCHIO_TC");
     if ((v && v[0] == '0') || !tc_driver_ready() || c->L.empty()) return PC_OK;
+    // expert GEMMs (INT4 experts)
+    if (c->eg.gu.fmt == TF_T4 && c->eg.dn.fmt == TF_T4 && c->eg.gu.blk_bytes <= 768 && c->eg.dn.blk_bytes <= 768 &&
+        c->eg.gu.Ip % 64 == 0 && c->eg.dn.Ip % 64 == 0) {
+        const int pairs = c->maxm * c->cfg.topk;
+        PC_TRY(dalloc(c, (size_t)(c->cfg.n_experts + 1) * 4, (void **)&c->pair_start));
+        PC_TRY(dalloc(c, (size_t)pairs * 4, (void **)&c->pair_list));
+        const cudaError_t e = tc_exp_init(c->tex, pairs, std::max(c->eg.gu.Ip, c->eg.dn.Ip));
+        if (c->tex.xg) c->allocs.push_back(c->tex.xg);
+        if (e != cudaSuccess) return cuda_fail(e, "tc_exp_init");
+    }
+    // dense projections (INT8)
     bool ok = c->lm_head.t.fmt == TF_T8;
     for (auto &ly : c->L)
         ok = ok && ly.wq.t.fmt == TF_T8 && ly.wk.t.fmt == TF_T8 && ly.wv.t.fmt == TF_T8 && ly.wo.t.fmt == TF_T8 &&
@@ -1093,11 +1171,16 @@ pc_status pc_get_logits(pc_ctx *c, int row, float *logits, int n) {
 // run_moe over M rows in chunks whose (row, k) pairs fit one router job table.
 pc_status run_moe_rows(pc_ctx *c, int layer, const float *x, int M, const int *sel, const float *w, float *out) {
     const int K = c->cfg.topk, D = c->cfg.hidden;
-    const int chunk = std::max(1, GEMV_MAX_JOBS / K);
-    for (int off = 0; off < M; off += chunk) {
-        const int m = std::min(chunk, M - off);
+    // chunks whose pairs fit one router launch: the expert-sorted lists of the
+    // tensor-core path hold more than the GEMV's job table
+    const bool tc = c->tex.on && (int64_t)M * K >= (int64_t)TE_MIN_PAIRS * c->cfg.n_experts;
+    const int chunk = std::max(1, (tc ? ROUTER_MAX_PAIRS : GEMV_MAX_JOBS) / K);
+    for (int off = 0; off < M;) {
+        int m = std::min(chunk, M - off);
+        if ((int64_t)m * K < (int64_t)TE_MIN_PAIRS * c->cfg.n_experts) m = std::min(m, std::max(1, GEMV_MAX_JOBS / K));
         PC_TRY(run_moe(c, layer, x + (size_t)off * D, m, sel ? sel + (size_t)off * K : nullptr,
                        w ? w + (size_t)off * K : nullptr, 0, out + (size_t)off * D, nullptr));
+        off += m;
     }
     return PC_OK;
 }

@@ -1,6 +1,6 @@
-// ptx.cuh - thin inline-PTX helpers for sm_100a: mbarriers, bulk copies,
-// f16 tensor-core MMA and the nibble/byte to f16 conversions the dequant
-// GEMV uses.
+// ptx.cuh - thin inline-PTX helpers for sm_100a: mbarriers, cp.async copies,
+// named barriers, the s8 MMA and the nibble to signed-byte conversions the
+// dequant GEMV uses.
 #pragma once
 #include <cstdint>
 
@@ -41,32 +41,6 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
     return ok != 0;
 }
 
-// Bounded wait: gives up after `limit` polls (each poll may suspend the
-// thread for a hardware-chosen interval) and returns false.
-__device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity, uint32_t limit) {
-    for (uint32_t i = 0; i < limit; ++i)
-        if (mbar_try_wait(bar, parity)) return true;
-    return false;
-}
-
-__device__ __forceinline__ uint64_t l2_evict_first_policy() {
-    uint64_t pol;
-    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
-    return pol;
-}
-
-// Bulk (non-tensor) global -> shared copy completing on an mbarrier.  No
-// multicast: each CTA fetches its own bytes.  dst/src 16-byte aligned,
-// bytes a multiple of 16.
-__device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar,
-                                         uint64_t policy) {
-    asm volatile(
-        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint "
-        "[%0], [%1], %2, [%3], %4;" ::"r"(smem_u32(dst)),
-        "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
-        : "memory");
-}
-
 // Streaming 16/8-byte global loads (evict-first in L1 and L2: weight bytes
 // are read once per launch).
 __device__ __forceinline__ uint4 ldg_stream(const void *p) { return __ldcs(reinterpret_cast<const uint4 *>(p)); }
@@ -84,11 +58,6 @@ __device__ __forceinline__ void cp_async_wait() {
 }
 
 // Brings the 128-byte line holding p into L2; nothing waits for it.
-// Asks L2 for `bytes` bytes at p (16-byte aligned, a multiple of 16) with one
-// bulk request; no data is returned to the SM.
-__device__ __forceinline__ void bulk_prefetch_l2(const void *p, uint32_t bytes) {
-    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
-}
 __device__ __forceinline__ void prefetch_l2(const void *p) {
     asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
 }

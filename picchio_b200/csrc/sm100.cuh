@@ -42,6 +42,18 @@ __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, u
         "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
         : "memory");
 }
+// 1-D bulk copy global -> shared completing on bar (transaction bytes); no
+// multicast, no cache hint.  Both addresses 16-byte aligned, bytes a
+// multiple of 16.
+__device__ __forceinline__ void bulk_load(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     smem_u32(dst)),
+                 "l"(src), "r"(bytes), "r"(smem_u32(bar))
+                 : "memory");
+}
+// Makes this thread's generic-proxy writes to shared memory visible to the
+// async proxy (tcgen05.mma operands written with st.shared).
+__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap *map) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
@@ -107,6 +119,22 @@ __device__ __forceinline__ uint64_t sw128_desc(const void *tile) {
            | (2ull << 61);          // layout: 128-byte swizzle
 }
 
+// D[tmem] (+)= A[smem] x B[smem]^T, f16 x f16 -> f32, one CTA.
+__device__ __forceinline__ void tc_mma_f16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                           bool accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"((uint32_t)accumulate)
+        : "memory");
+}
+// Instruction descriptor: f16 x f16 -> f32, both operands K-major, M x N.
+__host__ __device__ constexpr uint32_t idesc_f16(int M, int N) {
+    return (1u << 4)                         // D format: f32
+           | ((uint32_t)(N >> 3) << 17)      // N / 8 (A, B format 0: f16)
+           | ((uint32_t)(M >> 4) << 24);     // M / 16
+}
 // Instruction descriptor: s8 x s8 -> s32, both operands K-major, M x N.
 __host__ __device__ constexpr uint32_t idesc_i8(int M, int N) {
     return (2u << 4)                         // D format: s32

@@ -371,6 +371,319 @@ __global__ void tc_copy_t8_kernel(const uint8_t *tiles, int kblocks, int Op, int
     }
 }
 
+// ------------------------------------------------------------ expert GEMMs ----
+// One CTA: 128 weight rows (8 row tiles) of one expert's matrix x that
+// expert's pairs, TE_N at a time.  Warp 0 copies the raw INT4 blocks (1-D bulk
+// copies, one per row tile and 64-column step) into a TE_RR-deep ring; warps
+// 1-8 dequantize a step into the 128-byte-swizzled f16 A tile ((n - 8) *
+// scale in fp32, as the reference dequantizes, then rounded to f16) and run
+// the epilogue; warp 10 loads the pairs' f16 input rows with 2-D TMA; warp 9
+// allocates TMEM and issues tcgen05.mma kind::f16 (K = 16) into one f32
+// accumulator.  Every wait is bounded.
+constexpr int TE_RR = 8;                 // raw ring depth (64-column steps)
+constexpr int TE_S = 3;                  // f16 A / B stages
+constexpr int TE_RAW = 8 * 768;          // raw slot: 8 blocks of at most 768 bytes (gs16)
+constexpr int TE_A = 128 * 128;          // f16 A tile: 128 rows x 64 columns
+constexpr int TE_B = TE_N * 128;         // f16 B tile: TE_N rows x 64 columns
+constexpr int TE_DQ = 256;                // dequantizing (and epilogue) threads: warps 1-8
+constexpr int TE_THREADS = 32 * (TE_DQ / 32 + 3);  // + raw producer, MMA, B producer
+constexpr int TE_SMEM = 1024 + TE_S * (TE_A + TE_B) + TE_RR * TE_RAW + 512 + 4 * TE_N;
+
+// byte offset of (row, 4-column group at col) in a 128-byte-swizzled K-major
+// tile with 128-byte rows (col a multiple of 4)
+__device__ __forceinline__ uint32_t sw128_off(int row, int col) {
+    return (uint32_t)((row >> 3) * 1024 + (row & 7) * 128 + ((((col >> 3) ^ (row & 7)) << 4) | ((col & 7) * 2)));
+}
+
+__device__ __forceinline__ uint32_t pack_h2(float a, float b) {
+    const __half2 h = __floats2half2_rn(a, b);
+    return *reinterpret_cast<const uint32_t *>(&h);
+}
+
+// Dequantizes lane L's 16 bytes of one T4 block (rows g, g + 8; columns
+// 32m + 16h + 4t + j) into the f16 tile at row tile r.
+template <int GS>
+__device__ __forceinline__ void te_dequant_chunk(const uint8_t *blk, int L, int r, uint8_t *A) {
+    const int g = L >> 2, t = L & 3;
+    const uint4 w4 = *reinterpret_cast<const uint4 *>(blk + L * 16);
+    const uint32_t w[4] = {w4.x, w4.y, w4.z, w4.w};
+    float sc[4][2];  // [16-column group q][row half]
+    if (GS == 32) {
+        const float4 s = *reinterpret_cast<const float4 *>(blk + 512 + g * 16);
+        sc[0][0] = sc[1][0] = s.x; sc[0][1] = sc[1][1] = s.y;
+        sc[2][0] = sc[3][0] = s.z; sc[2][1] = sc[3][1] = s.w;
+    } else if (GS == 64) {
+        const float2 s = *reinterpret_cast<const float2 *>(blk + 512 + g * 8);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) { sc[q][0] = s.x; sc[q][1] = s.y; }
+    } else if (GS == 16) {
+        const float4 s0 = *reinterpret_cast<const float4 *>(blk + 512 + g * 32);
+        const float4 s1 = *reinterpret_cast<const float4 *>(blk + 512 + g * 32 + 16);
+        sc[0][0] = s0.x; sc[0][1] = s0.y; sc[1][0] = s0.z; sc[1][1] = s0.w;
+        sc[2][0] = s1.x; sc[2][1] = s1.y; sc[3][0] = s1.z; sc[3][1] = s1.w;
+    } else {  // per-row scale: applied in the epilogue
+#pragma unroll
+        for (int q = 0; q < 4; ++q) { sc[q][0] = 1.0f; sc[q][1] = 1.0f; }
+    }
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {  // word q = 2m + h
+        const int col = 32 * (q >> 1) + 16 * (q & 1) + 4 * t;
+#pragma unroll
+        for (int rh = 0; rh < 2; ++rh) {
+            const uint32_t wq = w[q] >> (4 * rh);
+            float v[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                // n - 8 exactly: the float 2^23 + n, minus 2^23 + 8
+                const float nf = __fsub_rn(__uint_as_float(((wq >> (8 * j)) & 0xFu) | 0x4B000000u), 8388616.0f);
+                v[j] = __fmul_rn(nf, sc[q][rh]);
+            }
+            const int row = r * 16 + g + 8 * rh;
+            *reinterpret_cast<uint2 *>(A + sw128_off(row, col)) = make_uint2(pack_h2(v[0], v[1]), pack_h2(v[2], v[3]));
+        }
+    }
+}
+
+template <int GS>
+__global__ void __launch_bounds__(TE_THREADS, 1) tc_exp_kernel(const __grid_constant__ TcExpParams p) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+    uint8_t *Abuf = smem, *Bbuf = smem + TE_S * TE_A, *Raw = Bbuf + TE_S * TE_B;
+    uint64_t *raw_full = reinterpret_cast<uint64_t *>(Raw + TE_RR * TE_RAW);
+    uint64_t *raw_empty = raw_full + TE_RR;
+    uint64_t *a_full = raw_empty + TE_RR;
+    uint64_t *b_full = a_full + TE_S;
+    uint64_t *st_empty = b_full + TE_S;
+    uint64_t *accf = st_empty + TE_S;      // accumulator of column tile ct complete
+    uint64_t *acce = accf + 1;             // ... and read out (TMEM free for the next)
+    uint32_t *tslot = reinterpret_cast<uint32_t *>(acce + 1);
+    int *cpair = reinterpret_cast<int *>(Raw + TE_RR * TE_RAW + 512);  // [TE_N] pair of each column
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int e = p.e_lo + blockIdx.y, rt0 = blockIdx.x * 8;
+
+    pdl_wait();  // the pair lists come from the router, the rows from the gather
+    pdl_trigger();
+    const int pbeg = __ldcg(p.pair_start + e), npair = __ldcg(p.pair_start + e + 1) - pbeg;
+    if (npair <= 0) return;  // uniform: no barrier or TMEM touched yet
+    const int nct = (npair + TE_N - 1) / TE_N;  // column tiles, in turn
+    const int nk = p.kblocks;
+    const uint8_t *tiles = p.table + (int64_t)(e - p.e_lo) * p.stride + p.off_tiles;
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < TE_RR; ++i) {
+            mbar_init(&raw_full[i], 1);
+            mbar_init(&raw_empty[i], TE_DQ);
+        }
+        for (int i = 0; i < TE_S; ++i) {
+            mbar_init(&a_full[i], TE_DQ);
+            mbar_init(&b_full[i], 1);
+            mbar_init(&st_empty[i], 1);
+        }
+        mbar_init(accf, 1);
+        mbar_init(acce, TE_DQ);
+        mbar_init_fence();
+    }
+    constexpr int W_MMA = TE_DQ / 32 + 1, W_B = TE_DQ / 32 + 2;
+    if (warp == W_MMA) {
+        tmem_alloc(tslot, TE_N);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tbase = *tslot;
+    const int nsteps = nct * nk;  // step ig = ct * nk + i
+
+    if (warp == 0) {
+        if (lane == 0) {  // raw INT4 blocks (re-read for every column tile)
+            int issued = 0;
+            for (int ig = 0; ig < nsteps; ++ig) {
+                const int i = ig % nk, sl = ig % TE_RR;
+                if (ig >= TE_RR && !mbar_wait(&raw_empty[sl], ((ig / TE_RR) - 1) & 1, TC_WAIT_NS)) {
+                    tc_fail(p.err, 3);
+                    break;
+                }
+                issued = ig + 1;
+                int nb = 0;
+                for (int r = 0; r < 8; ++r) nb += rt0 + r < p.n_rt;
+                mbar_arrive_expect_tx(&raw_full[sl], (uint32_t)(nb * p.blk_bytes));
+                for (int r = 0; r < 8; ++r)
+                    if (rt0 + r < p.n_rt)
+                        bulk_load(Raw + sl * TE_RAW + r * p.blk_bytes,
+                                  tiles + ((int64_t)(rt0 + r) * nk + i) * p.blk_bytes, (uint32_t)p.blk_bytes,
+                                  &raw_full[sl]);
+            }
+            // every copy issued has landed before the CTA can exit (already
+            // true unless a wait above gave up)
+            for (int j = max(0, issued - TE_RR); j < issued; ++j)
+                mbar_wait(&raw_full[j % TE_RR], (j / TE_RR) & 1, TC_WAIT_NS);
+        }
+    } else if (warp == W_B) {
+        if (lane == 0) {  // f16 input rows
+            tma_prefetch_desc(&p.bmap);
+            int issued = 0;
+            for (int ig = 0; ig < nsteps; ++ig) {
+                const int i = ig % nk, ct = ig / nk, s = ig % TE_S;
+                if (ig >= TE_S && !mbar_wait(&st_empty[s], ((ig / TE_S) - 1) & 1, TC_WAIT_NS)) {
+                    tc_fail(p.err, 3);
+                    break;
+                }
+                issued = ig + 1;
+                mbar_arrive_expect_tx(&b_full[s], TE_B);
+                tma_load_2d(Bbuf + s * TE_B, &p.bmap, &b_full[s], i * 64, pbeg + ct * TE_N);
+            }
+            for (int j = max(0, issued - TE_S); j < issued; ++j)
+                mbar_wait(&b_full[j % TE_S], (j / TE_S) & 1, TC_WAIT_NS);
+        }
+    } else if (warp == W_MMA) {
+        if (lane == 0) {  // MMA issuer
+            constexpr uint32_t idesc = idesc_f16(128, TE_N);
+            bool ok = true;
+            for (int ct = 0; ct < nct && ok; ++ct) {
+                // the previous tile's accumulator has been read out
+                if (ct > 0 && !mbar_wait(acce, (ct - 1) & 1, TC_WAIT_NS)) {
+                    tc_fail(p.err, 3);
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                for (int i = 0; i < nk; ++i) {
+                    const int ig = ct * nk + i, s = ig % TE_S;
+                    if (!mbar_wait(&a_full[s], (ig / TE_S) & 1, TC_WAIT_NS) ||
+                        !mbar_wait(&b_full[s], (ig / TE_S) & 1, TC_WAIT_NS)) {
+                        tc_fail(p.err, 3);
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint64_t ad = sw128_desc(Abuf + s * TE_A), bd = sw128_desc(Bbuf + s * TE_B);
+#pragma unroll
+                    for (int kk = 0; kk < 4; ++kk)
+                        tc_mma_f16(tbase, ad + 2 * kk, bd + 2 * kk, idesc, i > 0 || kk > 0);
+                    tc_commit(&st_empty[s]);
+                }
+                tc_commit(accf);  // fires once every MMA above has completed
+            }
+            if (!ok) tc_commit(accf);
+        }
+    } else {  // warps 1-8: dequantize every step; the epilogue after each column tile
+        const int td = threadIdx.x - 32;
+        // epilogue: lane quarter q of TMEM (warp % 4), column half ch
+        const int q = warp & 3, tr = 32 * q + lane, ch = (warp - 1) >> 2;
+        const int rt = rt0 + (tr >> 4), t16 = tr & 15;
+        const int o = tile_row_to_logical(p.perm, 0, rt, t16);
+        const bool rv = rt < p.n_rt && o < p.O;
+        const uint8_t *eb = p.table + (int64_t)(e - p.e_lo) * p.stride;
+        const float rs = (rv && p.off_rs >= 0) ? reinterpret_cast<const float *>(eb + p.off_rs)[o] : 1.0f;
+        const float bias = (rv && p.off_bias >= 0) ? reinterpret_cast<const float *>(eb + p.off_bias)[o] : 0.0f;
+        const uint32_t tl = tbase + ((uint32_t)(32 * q) << 16);
+        bool ok = true;
+        for (int ct = 0; ct < nct; ++ct) {
+            for (int i = 0; i < nk && ok; ++i) {
+                const int ig = ct * nk + i, sl = ig % TE_RR, s = ig % TE_S;
+                if (!mbar_wait(&raw_full[sl], (ig / TE_RR) & 1, TC_WAIT_NS) ||
+                    (ig >= TE_S && !mbar_wait(&st_empty[s], ((ig / TE_S) - 1) & 1, TC_WAIT_NS))) {
+                    tc_fail(p.err, 3);
+                    ok = false;
+                    break;
+                }
+                uint8_t *A = Abuf + s * TE_A;
+#pragma unroll
+                for (int k = 0; k < 256 / TE_DQ; ++k) {
+                    const int c = td + TE_DQ * k, r = c >> 5, L = c & 31;
+                    if (rt0 + r < p.n_rt) {
+                        te_dequant_chunk<GS>(Raw + sl * TE_RAW + r * p.blk_bytes, L, r, A);
+                    } else {  // rows past the matrix: zero
+                        const int g = L >> 2, t = L & 3;
+#pragma unroll
+                        for (int w = 0; w < 4; ++w)
+#pragma unroll
+                            for (int rh = 0; rh < 2; ++rh)
+                                *reinterpret_cast<uint2 *>(
+                                    A + sw128_off(r * 16 + g + 8 * rh, 32 * (w >> 1) + 16 * (w & 1) + 4 * t)) =
+                                    make_uint2(0u, 0u);
+                    }
+                }
+                fence_async_smem();
+                mbar_arrive(&a_full[s]);
+                mbar_arrive(&raw_empty[sl]);
+            }
+            // epilogue of column tile ct: thread = TMEM lane = weight row of the tile
+            const int c0 = ct * TE_N, ncols = min(TE_N, npair - c0);
+            if (td < TE_N) cpair[td] = td < ncols ? __ldcg(p.pair_list + pbeg + c0 + td) : 0;
+            named_bar_sync(1, TE_DQ);
+            if (!mbar_wait(accf, ct & 1, TC_WAIT_NS)) {
+                tc_fail(p.err, 3);
+                ok = false;
+            }
+            __syncwarp();
+            tc_fence_after();
+            constexpr int CH = TE_N * 128 / TE_DQ;  // columns per warp (TE_DQ / 128 warps per lane quarter)
+            for (int cc = ch * CH; cc < (ch + 1) * CH; cc += 16) {
+                uint32_t d[16];
+                tmem_ld16(tl + cc, d);
+                tmem_ld_wait();
+                float x[16];
+#pragma unroll
+                for (int j = 0; j < 16; ++j) {
+                    float v = __uint_as_float(d[j]);
+                    if (p.off_rs >= 0) v = __fmul_rn(v, rs);
+                    if (p.off_bias >= 0) v = __fadd_rn(v, bias);
+                    x[j] = v;
+                }
+                if (p.epi == EPI_SWIGLU) {
+                    // gate = tile row g (logical 2i), up = g + 8 (2i + 1): lanes l, l ^ 8
+                    float up[16];
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) up[j] = __shfl_xor_sync(0xffffffffu, x[j], 8);
+                    if (ok && rv && t16 < 8 && (o + 1) < p.O) {
+#pragma unroll
+                        for (int j = 0; j < 16; ++j) {
+                            const int n = cc + j;
+                            if (n < ncols)
+                                p.y[(int64_t)cpair[n] * p.ldy + (o >> 1)] =
+                                    swiglu(x[j], up[j], p.swiglu_limit, p.swiglu_alpha);
+                        }
+                    }
+                } else if (ok && rv) {
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) {
+                        const int n = cc + j;
+                        if (n < ncols) p.y[(int64_t)cpair[n] * p.ldy + o] = x[j];
+                    }
+                }
+            }
+            tc_fence_before();
+            named_bar_sync(1, TE_DQ);  // every lane's reads done; cpair free
+            mbar_arrive(acce);
+            if (!ok) break;
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == W_MMA) {
+        __syncwarp();
+        tc_fence_after();
+        tmem_dealloc(tbase, TE_N);
+    }
+}
+
+// One block per sorted pair slot: that pair's input row to f16 (zero past I).
+__global__ void tc_exp_gather_kernel(const float *x, int ldx, int I, int K, int by_pair, const int *pair_start,
+                                     const int *pair_list, int E, int Kp, __half *xg) {
+    pdl_wait();
+    pdl_trigger();
+    const int qi = blockIdx.x;
+    if (qi >= __ldcg(pair_start + E)) return;
+    const int pr = __ldcg(pair_list + qi);
+    const float *src = x + (int64_t)(by_pair ? pr : pr / K) * ldx;
+    __half2 *dst = reinterpret_cast<__half2 *>(xg + (int64_t)qi * Kp);
+    for (int c = threadIdx.x * 2; c < Kp; c += blockDim.x * 2) {
+        const float a = c < I ? src[c] : 0.0f, b = c + 1 < I ? src[c + 1] : 0.0f;
+        dst[c >> 1] = __floats2half2_rn(a, b);
+    }
+}
+
 typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
                                   const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
@@ -465,6 +778,54 @@ size_t tc_part_bytes(int tiles, int nsplit, int M) {
     if (nsplit <= 1) return 0;
     const int N = M <= 32 ? 32 : M <= 64 ? 64 : 128;
     return (size_t)tiles * N * 128 * 8;
+}
+
+cudaError_t tc_exp_init(TcExpState &s, int max_pairs, int max_kp) {
+    s.rows = max_pairs;
+    s.Kp = (max_kp + 63) / 64 * 64;
+    cudaError_t e = cudaMalloc(&s.xg, (size_t)s.rows * s.Kp * 2);
+    if (e == cudaSuccess) e = cudaMemset(s.xg, 0, (size_t)s.rows * s.Kp * 2);
+    if (e != cudaSuccess) return e;
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return cudaErrorNotSupported;
+    const cuuint64_t dims[2] = {(cuuint64_t)s.Kp, (cuuint64_t)s.rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)s.Kp * 2};
+    const cuuint32_t box[2] = {64u, (cuuint32_t)TE_N};
+    const cuuint32_t es[2] = {1u, 1u};
+    const CUresult r = fn(&s.bmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, s.xg, dims, strides, box, es,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return cudaErrorInvalidValue;
+    for (int gs : {0, 16, 32, 64}) {
+        cudaError_t a = cudaSuccess;
+        if (gs == 0) a = cudaFuncSetAttribute(tc_exp_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, TE_SMEM);
+        if (gs == 16) a = cudaFuncSetAttribute(tc_exp_kernel<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, TE_SMEM);
+        if (gs == 32) a = cudaFuncSetAttribute(tc_exp_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, TE_SMEM);
+        if (gs == 64) a = cudaFuncSetAttribute(tc_exp_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, TE_SMEM);
+        if (a != cudaSuccess) return a;
+    }
+    s.on = true;
+    return cudaSuccess;
+}
+
+cudaError_t tc_exp_gather(const TcExpState &s, const float *x, int ldx, int I, int K, bool by_pair,
+                          const int *pair_start, const int *pair_list, int E, int max_pairs, cudaStream_t st) {
+    if (max_pairs > s.rows || I > s.Kp) return cudaErrorInvalidValue;
+    return launch_k(tc_exp_gather_kernel, dim3(max_pairs), dim3(256), 0, st, x, ldx, I, K, (int)by_pair, pair_start,
+                    pair_list, E, s.Kp, s.xg);
+}
+
+cudaError_t tc_exp_launch(const TcExpParams &p, int gs, int n_local, int max_pairs, cudaStream_t st) {
+    if (p.blk_bytes > 768 || p.Ip % 64) return cudaErrorInvalidValue;
+    (void)max_pairs;
+    const dim3 grid((p.n_rt + 7) / 8, n_local);
+    switch (gs) {
+        case 0: return launch_k(tc_exp_kernel<0>, grid, dim3(TE_THREADS), TE_SMEM, st, p);
+        case 16: return launch_k(tc_exp_kernel<16>, grid, dim3(TE_THREADS), TE_SMEM, st, p);
+        case 32: return launch_k(tc_exp_kernel<32>, grid, dim3(TE_THREADS), TE_SMEM, st, p);
+        case 64: return launch_k(tc_exp_kernel<64>, grid, dim3(TE_THREADS), TE_SMEM, st, p);
+    }
+    return cudaErrorInvalidValue;
 }
 
 cudaError_t tc_launch(TcParams &p, int M, cudaStream_t st) {

@@ -3,6 +3,7 @@
 // 16..128 rows at once on tcgen05 s8 x s8 -> s32 MMAs.
 #pragma once
 #include <cuda.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
 #include <cstdint>
@@ -73,6 +74,43 @@ struct TcState {
     unsigned *ctr = nullptr;
     int ctr_n = 0;
 };
+
+// ---- expert GEMMs on the tensor cores (many input rows per expert) --------
+// One launch = one expert matrix (gate_up or down) of every resident expert
+// over that expert's (token, k) pairs: INT4 tiles dequantized to f16 in
+// shared memory ((n - 8) * scale rounded once), input rows gathered and
+// rounded to f16, tcgen05 f16 x f16 -> f32 MMAs.
+constexpr int TE_N = 128;            // pairs per CTA (MMA N)
+constexpr int TE_MIN_PAIRS = 32;     // average pairs per expert from which run_moe uses this path
+
+struct TcExpParams {
+    const uint8_t *table;            // the layer's expert table
+    int64_t stride;                  // bytes per expert
+    int64_t off_tiles, off_rs, off_bias;  // within an expert; -1 = absent
+    int kblocks, blk_bytes, n_rt, O, Ip;  // T4 tile geometry of this matrix
+    int e_lo, e_hi;                  // resident experts (table slot = e - e_lo)
+    const int *pair_start, *pair_list;  // from the router: pairs sorted by expert
+    CUtensorMap bmap;                // gathered f16 input rows [pairs][Ip], box 64 x TE_N
+    int epi, perm;                   // EPI_SWIGLU (gate_up, PERM_PAIR) or EPI_STORE (down)
+    float *y;                        // output row = pair index
+    int ldy;
+    float swiglu_limit, swiglu_alpha;
+    int *err;
+};
+
+struct TcExpState {
+    bool on = false;
+    int rows = 0, Kp = 0;            // capacity: pairs x padded input length
+    __half *xg = nullptr;            // [rows][Kp]
+    CUtensorMap bmap;
+};
+
+cudaError_t tc_exp_init(TcExpState &s, int max_pairs, int max_kp);
+// Gathers the input row of every pair (down: row = pair index; otherwise row
+// = pair / K) in expert order into s.xg, rounded to f16, zero past I.
+cudaError_t tc_exp_gather(const TcExpState &s, const float *x, int ldx, int I, int K, bool by_pair,
+                          const int *pair_start, const int *pair_list, int E, int max_pairs, cudaStream_t st);
+cudaError_t tc_exp_launch(const TcExpParams &p, int gs, int n_local_experts, int max_pairs, cudaStream_t st);
 
 // Resolves cuTensorMapEncodeTiled through the runtime (no link-time driver
 // dependency); false when it is unavailable.

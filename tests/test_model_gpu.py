@@ -173,6 +173,30 @@ def test_moe_forward_against_oracle(variant):
                     assert rel_l2(out[r], ref) < 1e-5, (M, layer, r)
 
 
+def test_moe_forward_tensor_core_experts_against_oracle(variant):
+    """256 rows x top-2 of 8 experts = 64 pairs per expert: the expert GEMMs
+    run on the tensor cores (INT4 dequantized to f16, inputs rounded to f16,
+    f32 accumulation; 6 launches instead of the GEMV path's 4).  Within
+    2e-3 relative L2 of the oracle per row (f16 rounding of weights and
+    inputs, ~5e-4 each)."""
+    import torch
+    from picchio_b200 import Model
+    m, d = variant
+    orc = O.OracleModel(d, ctx=64)
+    rng = np.random.default_rng(4)
+    D, M = orc.c.hidden, 256
+    x = rng.standard_normal((M, D)).astype(np.float32)
+    with Model(d, ctx=64, max_batch=M) as model:
+        for layer in range(orc.c.n_layers):
+            n0 = model.launches
+            out = model.moe_forward(torch.from_numpy(x).cuda(), layer).cpu().numpy()
+            assert model.launches - n0 == 6
+            worst = 0.0
+            for r in range(0, M, 7):
+                worst = max(worst, rel_l2(out[r], orc.moe(x[r], layer)))
+            assert worst < 2e-3, (layer, worst)
+
+
 def test_range_errors(variant):
     from picchio_b200 import Model, PicchioError
     m, d = variant
@@ -285,8 +309,10 @@ def test_long_context_multi_span_attention_matches_oracle():
 
 def test_batched_rows_attention_matches_single_row():
     """128 sequences with 600 seeded cache positions each (3 spans per row in
-    the full layers, 768 span CTAs per layer): batch row 0's next id and
-    logits equal those of the same sequence decoded alone."""
+    the full layers, 768 span CTAs per layer): batch row 0's next id equals
+    that of the same sequence decoded alone, its logits within 2e-3 (with 32
+    pairs per expert the batch's expert GEMMs run on the tensor cores with f16
+    operands; the single sequence's on the exact-sum GEMV)."""
     from picchio_b200 import Model
     m = meta("tiny_gs32_i8")
     import tempfile
@@ -304,4 +330,4 @@ def test_batched_rows_attention_matches_single_row():
         t = a.forward_token(toks[0], n)
         la = a.logits(0)
     assert nxt[0] == t
-    assert rel_l2(lb, la) < 1e-5
+    assert rel_l2(lb, la) < 2e-3
