@@ -58,6 +58,20 @@ __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap *map) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
 
+// ------------------------------------------------------- packed fp32 ----
+// Two fp32 lanes per 64-bit register (low word = first), one instruction
+// each: sub.rn.f32x2 / mul.rn.f32x2 round every lane as sub.rn / mul.rn do.
+__device__ __forceinline__ uint64_t f2_sub(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+
 // ---------------------------------------------------------------- tcgen05 ----
 // TMEM allocation: one full warp; the base address is written to *slot.
 __device__ __forceinline__ void tmem_alloc(uint32_t *slot, uint32_t ncols) {

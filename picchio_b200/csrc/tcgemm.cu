@@ -379,9 +379,11 @@ __global__ void tc_copy_t8_kernel(const uint8_t *tiles, int kblocks, int Op, int
 // scale in fp32, as the reference dequantizes, then rounded to f16) and run
 // the epilogue; warp 10 loads the pairs' f16 input rows with 2-D TMA; warp 9
 // allocates TMEM and issues tcgen05.mma kind::f16 (K = 16) into one f32
-// accumulator.  Every wait is bounded.
-constexpr int TE_RR = 8;                 // raw ring depth (64-column steps)
-constexpr int TE_S = 3;                  // f16 A / B stages
+// accumulator.  Two CTAs share an SM (102 KB of shared memory and 128 TMEM
+// columns each), so one CTA's dequantization overlaps the other's waits and
+// epilogue.  Every wait is bounded.
+constexpr int TE_RR = 6;                 // raw ring depth (64-column steps)
+constexpr int TE_S = 2;                  // f16 A / B stages
 constexpr int TE_RAW = 8 * 768;          // raw slot: 8 blocks of at most 768 bytes (gs16)
 constexpr int TE_A = 128 * 128;          // f16 A tile: 128 rows x 64 columns
 constexpr int TE_B = TE_N * 128;         // f16 B tile: TE_N rows x 64 columns
@@ -400,8 +402,30 @@ __device__ __forceinline__ uint32_t pack_h2(float a, float b) {
     return *reinterpret_cast<const uint32_t *>(&h);
 }
 
+// Two nibble values held as the floats 2^23 + n (bytes [n, 0, 0, 0x4B]) to the
+// packed f16 pair of (n - 8) * s: exact subtraction, then one fp32 multiply
+// (the reference's dequantization), both as packed f32x2 operations, then
+// round to f16.
+__device__ __forceinline__ uint32_t te_dq2(uint32_t a, uint32_t b, uint64_t s2) {
+    uint64_t v;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(v) : "r"(a), "r"(b));
+    constexpr uint64_t MAGIC2 = 0x4B0000084B000008ull;  // 2^23 + 8 twice
+    v = f2_mul(f2_sub(v, MAGIC2), s2);
+    uint32_t lo, hi;
+    asm("mov.b64 {%0, %1}, %2;" : "=r"(lo), "=r"(hi) : "l"(v));
+    return pack_h2(__uint_as_float(lo), __uint_as_float(hi));
+}
+
+__device__ __forceinline__ uint64_t dup_f2(float s) {
+    uint64_t v;
+    asm("mov.b64 %0, {%1, %1};" : "=l"(v) : "r"(__float_as_uint(s)));
+    return v;
+}
+
 // Dequantizes lane L's 16 bytes of one T4 block (rows g, g + 8; columns
-// 32m + 16h + 4t + j) into the f16 tile at row tile r.
+// 32m + 16h + 4t + j) into the f16 tile at row tile r.  Byte j of word q holds
+// column 32m + 16h + 4t + j (q = 2m + h): row g in its low nibble, row g + 8
+// in its high nibble.
 template <int GS>
 __device__ __forceinline__ void te_dequant_chunk(const uint8_t *blk, int L, int r, uint8_t *A) {
     const int g = L >> 2, t = L & 3;
@@ -430,22 +454,19 @@ __device__ __forceinline__ void te_dequant_chunk(const uint8_t *blk, int L, int 
         const int col = 32 * (q >> 1) + 16 * (q & 1) + 4 * t;
 #pragma unroll
         for (int rh = 0; rh < 2; ++rh) {
-            const uint32_t wq = w[q] >> (4 * rh);
-            float v[4];
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                // n - 8 exactly: the float 2^23 + n, minus 2^23 + 8
-                const float nf = __fsub_rn(__uint_as_float(((wq >> (8 * j)) & 0xFu) | 0x4B000000u), 8388616.0f);
-                v[j] = __fmul_rn(nf, sc[q][rh]);
-            }
+            const uint32_t nib = (w[q] >> (4 * rh)) & 0x0F0F0F0Fu;  // byte j = n of column j
+            // byte j of nib into byte 0, zeros, 0x4B into byte 3: the float 2^23 + n
+            const uint32_t f0 = __byte_perm(nib, 0x4B000000u, 0x7540), f1 = __byte_perm(nib, 0x4B000000u, 0x7541);
+            const uint32_t f2 = __byte_perm(nib, 0x4B000000u, 0x7542), f3 = __byte_perm(nib, 0x4B000000u, 0x7543);
+            const uint64_t s2 = dup_f2(sc[q][rh]);
             const int row = r * 16 + g + 8 * rh;
-            *reinterpret_cast<uint2 *>(A + sw128_off(row, col)) = make_uint2(pack_h2(v[0], v[1]), pack_h2(v[2], v[3]));
+            *reinterpret_cast<uint2 *>(A + sw128_off(row, col)) = make_uint2(te_dq2(f0, f1, s2), te_dq2(f2, f3, s2));
         }
     }
 }
 
 template <int GS>
-__global__ void __launch_bounds__(TE_THREADS, 1) tc_exp_kernel(const __grid_constant__ TcExpParams p) {
+__global__ void __launch_bounds__(TE_THREADS, 2) tc_exp_kernel(const __grid_constant__ TcExpParams p) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
     uint8_t *Abuf = smem, *Bbuf = smem + TE_S * TE_A, *Raw = Bbuf + TE_S * TE_B;
@@ -537,9 +558,11 @@ __global__ void __launch_bounds__(TE_THREADS, 1) tc_exp_kernel(const __grid_cons
         }
     } else if (warp == W_MMA) {
         if (lane == 0) {  // MMA issuer
-            constexpr uint32_t idesc = idesc_f16(128, TE_N);
             bool ok = true;
             for (int ct = 0; ct < nct && ok; ++ct) {
+                // N: this tile's pairs rounded up to 16 (the B rows past them are
+                // other experts' pairs or zero fill; their columns are not read)
+                const uint32_t idesc = idesc_f16(128, min(TE_N, (npair - ct * TE_N + 15) & ~15));
                 // the previous tile's accumulator has been read out
                 if (ct > 0 && !mbar_wait(acce, (ct - 1) & 1, TC_WAIT_NS)) {
                     tc_fail(p.err, 3);
