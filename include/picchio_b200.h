@@ -111,23 +111,29 @@ void pc_free(pc_ctx *ctx);
 pc_status pc_get_config(const pc_ctx *ctx, pc_model_cfg *cfg);
 
 /* One decode step: replaces forward_token (picchio.c:1655-1756) with greedy
- * sampling (sample_logits at TEMPERATURE=0, picchio.c:1555-1560).  Writes the
- * next id to *next_tok.  tok outside [0, vocab) embeds as zeros like
- * embed_token (picchio.c:1478-1481). */
+ * sampling (sample_logits at TEMPERATURE=0, picchio.c:1555-1560), or the
+ * device draw when pc_set_sampling is on.  Writes the next id to *next_tok.
+ * tok outside [0, vocab) embeds as zeros like embed_token
+ * (picchio.c:1478-1481). */
 pc_status pc_forward_token(pc_ctx *ctx, int tok, int pos, int *next_tok);
 
-/* Prompt encoding: replaces prefill_tokens (picchio.c:1936-1975).  Returns
- * the greedy id after the last position. */
+/* Prompt encoding: replaces prefill_tokens (picchio.c:1936-1975) in blocks
+ * of 64 positions.  Returns the greedy id after the last position, or, with
+ * device sampling on (pc_set_sampling), the id drawn there; like the
+ * reference's forward_prefill, every block then draws (and records) one id.
+ * The repetition history is seeded by the caller (pc_history_push), as
+ * prefill_tokens seeds g_history before its blocks (picchio.c:1963-1967). */
 pc_status pc_prefill(pc_ctx *ctx, const int *ids, int n, int pos_base, int *next_tok);
 
 /* B independent sequences, one token each (sequence b uses KV slot b): the
  * batched-decode form of forward_token.  B <= opts.max_batch. */
 pc_status pc_decode_batch(pc_ctx *ctx, const int *toks, const int *pos, int B, int *next);
 
-/* Greedy decode of n steps of one sequence without host round trips: the
- * decode loop of picchio's main (picchio.c:3212-3287) at TEMPERATURE=0.
- * Step i feeds the id of step i-1 (tok for i = 0) at position pos + i;
- * out_ids[i] receives its greedy next id.  *device_ms (optional) receives
+/* Decode of n steps of one sequence without host round trips: the decode
+ * loop of picchio's main (picchio.c:3212-3287), greedy (TEMPERATURE=0) or
+ * with the device draw when pc_set_sampling is on.  Step i feeds the id of
+ * step i-1 (tok for i = 0) at position pos + i; out_ids[i] receives its next
+ * id.  *device_ms (optional) receives
  * the device time of the n steps, from CUDA events on the context stream. */
 pc_status pc_generate(pc_ctx *ctx, int tok, int pos, int n, int *out_ids, float *device_ms);
 
@@ -139,6 +145,41 @@ pc_status pc_kv_fill_synthetic(pc_ctx *ctx, int seq, int n_pos, uint64_t seed);
 
 /* Copies the logits of the last step (row `row` of a batch) to the host. */
 pc_status pc_get_logits(pc_ctx *ctx, int row, float *logits, int n);
+
+/* Sampling settings of sample_logits (picchio.c:1540-1649; the globals
+ * g_temperature, g_top_p, g_top_k, g_rep_penalty of picchio.c:1510-1513). */
+typedef struct {
+    float temperature; /* below 1e-6: argmax of the penalized logits */
+    float top_p;       /* nucleus mass; active in (0, 1) */
+    int top_k;         /* active in (0, vocab) */
+    float rep_penalty; /* active above 1: ids in the history are penalized */
+} pc_sampling;
+
+/* Replaces the host-side sample_logits (picchio.c:1540-1649) with a device
+ * draw for every later single-sequence step (pc_forward_token, pc_prefill,
+ * pc_generate): the next id is drawn from the step's logits on the device,
+ * recorded in the device history and returned, with no logits copy.  NULL
+ * restores the default (plain argmax, no history).  Batched decode
+ * (pc_decode_batch) stays greedy per row. */
+pc_status pc_set_sampling(pc_ctx *ctx, const pc_sampling *s);
+
+/* The xorshift64 generator state of the draws (g_rng, picchio.c:1520-1526). */
+pc_status pc_set_rng(pc_ctx *ctx, uint64_t state);
+pc_status pc_get_rng(pc_ctx *ctx, uint64_t *state);
+
+/* The repetition-penalty history (g_history, picchio.c:1516-1517; at most
+ * 4096 ids).  push appends ids in [0, vocab) and skips others, as
+ * prefill_tokens seeds it with the prompt (picchio.c:1963-1967); get copies
+ * up to cap ids and sets *n to the history length. */
+pc_status pc_history_reset(pc_ctx *ctx);
+pc_status pc_history_push(pc_ctx *ctx, const int *ids, int n);
+pc_status pc_history_get(pc_ctx *ctx, int *ids, int cap, int *n);
+
+/* One draw with the current settings from a device logits row of vocab
+ * floats (sample_logits itself, picchio.c:1540): advances the generator and
+ * appends the id to the history like the step's draw.  The logits are not
+ * modified. */
+pc_status pc_sample(pc_ctx *ctx, const float *logits_dev, int *id);
 
 /* The MoE block of one layer on M rows: replaces moe_forward
  * (picchio.c:1309-1466): router + top-k + softmax, gate_up + bias + clamped
@@ -159,10 +200,24 @@ pc_status pc_set_trace(pc_ctx *ctx, int on);
 pc_status pc_get_stage(pc_ctx *ctx, const char *name, float *out, int n);
 pc_status pc_dump(pc_ctx *ctx, const char *dir);  /* writes <name>.npy like ORACLE_DIR */
 
-/* Expert prefetch hint, the counterpart of prefetch_issue
- * (picchio.c:1180-1230).  Every expert is resident in HBM (the only residency
- * mode built), so this validates its arguments and returns PC_OK. */
+/* Expert residency (opts.expert_residency).  0: every expert in one HBM
+ * table.  1: the counterpart of the reference's expert cache (ESlot,
+ * cache_load_batch, LRU; picchio.c:121-136, 1000-1068) for expert tables
+ * larger than HBM: all experts in pinned, device-mapped host memory and
+ * opts.expert_cache_slots experts per layer in HBM.  A step reads a
+ * non-resident expert over the host link (never waits for the host); after
+ * the step the experts it read move into HBM slots, least recently used
+ * slot first.  Results are identical in both modes. */
+
+/* Makes the given experts of a layer resident in HBM now, the counterpart of
+ * cache_load_batch / prefetch_issue (picchio.c:1000-1068, 1180-1230); ids
+ * of other ranks or -1 are skipped.  PC_OK without work in mode 0. */
 pc_status pc_expert_prefetch(pc_ctx *ctx, int layer, const int *eids, int n);
+
+/* Residency counters since pc_init (the reference's cache hit/miss stats):
+ * experts read from HBM slots, experts read from the host, bytes copied
+ * into slots.  Any pointer may be NULL.  All zero in mode 0. */
+pc_status pc_expert_stats(pc_ctx *ctx, uint64_t *hits, uint64_t *misses, uint64_t *bytes_h2d);
 
 /* ---- weight-level operator: matmul_qt (quant.h:323-337) ---------------- */
 

@@ -325,3 +325,111 @@ OR_API int or_argmax(const float *logits, int n) {
     for (int i = 1; i < n; i++) if (logits[i] > logits[best]) best = i;
     return best;
 }
+
+/* ------------------------------------------------------------ sampling ---- */
+/* sample_logits (picchio.c:1540-1649) with the sampler's globals passed in:
+ * repetition penalty over the history (1542-1552), temperature (1555-1565),
+ * top-k with the k-th largest value as threshold and ties kept (1571-1581),
+ * softmax with expf (1584-1591), top-p over the probabilities above 1e-10
+ * sorted descending (1594-1627), then the draw from the xorshift64 generator
+ * (1520-1526, 1631-1647).  The reference leaves the order of EQUAL
+ * probabilities in its top-p sort to qsort; this restatement orders them by
+ * id, as the device sampler does.  logits are modified in place like the
+ * reference's; the history (at most 4096 ids) and the generator state are
+ * read and updated through the pointers. */
+typedef struct { float p; int id; } or_cand;
+
+static int or_desc_f(const void *a, const void *b) {
+    const float x = *(const float *)a, y = *(const float *)b;
+    return (x < y) - (x > y);
+}
+
+static int or_desc_cand(const void *a, const void *b) {
+    const or_cand *x = (const or_cand *)a, *y = (const or_cand *)b;
+    if (x->p != y->p) return x->p < y->p ? 1 : -1;
+    return (x->id > y->id) - (x->id < y->id);
+}
+
+static int or_keep(int *hist, int *hist_len, int id) {
+    if (*hist_len < 4096) hist[(*hist_len)++] = id;
+    return id;
+}
+
+OR_API int or_sample(float *lg, int V, float temperature, float top_p, int top_k, float rep,
+                     int *hist, int *hist_len, uint64_t *rng) {
+    if (rep > 1.0f)
+        for (int h = 0; h < *hist_len; ++h) {
+            const int t = hist[h];
+            if (t >= 0 && t < V) lg[t] = lg[t] > 0 ? lg[t] / rep : lg[t] * rep;
+        }
+    if (temperature < 1e-6f) {
+        int best = 0;
+        for (int i = 1; i < V; ++i)
+            if (lg[i] > lg[best]) best = i;
+        return or_keep(hist, hist_len, best);
+    }
+    const float inv = 1.0f / temperature;
+    for (int i = 0; i < V; ++i) lg[i] *= inv;
+    if (top_k > 0 && top_k < V) {
+        float *sorted = (float *)malloc((size_t)V * sizeof(float));
+        memcpy(sorted, lg, (size_t)V * sizeof(float));
+        qsort(sorted, (size_t)V, sizeof(float), or_desc_f);
+        const float th = sorted[top_k - 1];
+        free(sorted);
+        for (int i = 0; i < V; ++i)
+            if (lg[i] < th) lg[i] = -1e30f;
+    }
+    float mx = -1e30f;
+    for (int i = 0; i < V; ++i)
+        if (lg[i] > mx) mx = lg[i];
+    float sum = 0.0f;
+    for (int i = 0; i < V; ++i) {
+        lg[i] = expf(lg[i] - mx);
+        sum += lg[i];
+    }
+    for (int i = 0; i < V; ++i) lg[i] /= sum;
+    if (top_p < 1.0f && top_p > 0.0f) {
+        int n = 0;
+        for (int i = 0; i < V; ++i) n += lg[i] > 1e-10f;
+        if (n > 1) {
+            or_cand *c = (or_cand *)malloc((size_t)n * sizeof(or_cand));
+            n = 0;
+            for (int i = 0; i < V; ++i)
+                if (lg[i] > 1e-10f) {
+                    c[n].p = lg[i];
+                    c[n].id = i;
+                    ++n;
+                }
+            qsort(c, (size_t)n, sizeof(or_cand), or_desc_cand);
+            float cum = 0.0f;
+            int cut = n;
+            for (int j = 0; j < n; ++j) {
+                cum += c[j].p;
+                if (cum >= top_p) {
+                    cut = j + 1;
+                    break;
+                }
+            }
+            for (int j = cut; j < n; ++j) lg[c[j].id] = 0.0f;
+            float s2 = 0.0f;
+            for (int i = 0; i < V; ++i) s2 += lg[i];
+            if (s2 > 0)
+                for (int i = 0; i < V; ++i) lg[i] /= s2;
+            free(c);
+        }
+    }
+    uint64_t s = *rng;
+    s ^= s << 13;
+    s ^= s >> 7;
+    s ^= s << 17;
+    *rng = s;
+    const float r = (float)(s >> 33) / (float)(1ULL << 31);
+    float cum = 0.0f;
+    for (int i = 0; i < V; ++i) {
+        cum += lg[i];
+        if (cum >= r) return or_keep(hist, hist_len, i);
+    }
+    for (int i = V - 1; i >= 0; --i)
+        if (lg[i] > 0) return or_keep(hist, hist_len, i);
+    return 0;
+}

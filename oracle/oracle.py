@@ -75,6 +75,9 @@ def lib():
         L.or_axpy.argtypes = [_fp, _fp, C.c_float, C.c_int]
         L.or_argmax.argtypes = [_fp, C.c_int]
         L.or_argmax.restype = C.c_int
+        L.or_sample.argtypes = [_fp, C.c_int, C.c_float, C.c_float, C.c_int, C.c_float, _ip, _ip,
+                                C.POINTER(C.c_uint64)]
+        L.or_sample.restype = C.c_int
         _lib = L
     return _lib
 
@@ -98,6 +101,10 @@ def ref_lib():
         R.ref_yarn_inv_freq.argtypes = [C.c_int, C.c_float, C.c_float, C.c_float, C.c_float,
                                         C.c_int, C.c_int, C.c_int]
         R.ref_yarn_inv_freq.restype = C.c_float
+        if hasattr(R, "ref_sample_logits"):
+            R.ref_sample_logits.argtypes = [_fp, C.c_int, C.c_float, C.c_float, C.c_int, C.c_float, _ip, _ip,
+                                            C.POINTER(C.c_uint64)]
+            R.ref_sample_logits.restype = C.c_int
         _ref = R
     return _ref
 
@@ -187,6 +194,45 @@ def swiglu(gu, limit, alpha=1.702):
 
 def argmax(logits):
     return int(lib().or_argmax(_ptr(_f(logits), _fp), logits.size))
+
+
+class SamplerState:
+    """The sampler's mutable globals (picchio.c:1516-1520): the repetition
+    history (at most 4096 ids) and the xorshift64 state."""
+
+    def __init__(self, rng: int, history=()):
+        self.rng = int(rng)
+        self.history = [int(t) for t in history][:4096]
+
+    def copy(self):
+        return SamplerState(self.rng, self.history)
+
+
+def _sample_with(fn, logits, temperature, top_p, top_k, rep, state: SamplerState):
+    lg = _f(logits).copy()
+    hist = np.zeros(4096, np.int32)
+    hist[:len(state.history)] = state.history
+    hl = C.c_int(len(state.history))
+    rng = C.c_uint64(state.rng)
+    tid = int(fn(_ptr(lg, _fp), lg.size, float(temperature), float(top_p), int(top_k), float(rep),
+                 _ptr(hist, _ip), C.byref(hl), C.byref(rng)))
+    state.rng = int(rng.value)
+    state.history = hist[:hl.value].tolist()
+    return tid, lg
+
+
+def sample(logits, temperature, top_p, top_k, rep, state: SamplerState):
+    """sample_logits (picchio.c:1540-1649) restated (oracle.c or_sample):
+    returns (id, the logits array as the reference leaves it); updates state."""
+    return _sample_with(lib().or_sample, logits, temperature, top_p, top_k, rep, state)
+
+
+def ref_sample(logits, temperature, top_p, top_k, rep, state: SamplerState):
+    """The reference's own sample_logits (oracle/_ref), same contract as sample()."""
+    R = ref_lib()
+    if R is None or not hasattr(R, "ref_sample_logits"):
+        raise RuntimeError("the reference library is not built (oracle/_ref)")
+    return _sample_with(R.ref_sample_logits, logits, temperature, top_p, top_k, rep, state)
 
 
 # ----------------------------------------------------------------------------

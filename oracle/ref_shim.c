@@ -119,3 +119,22 @@ REF_API void ref_gqa_attention(const int8_t *wq, const float *sq, const int8_t *
     kv.K = Kp; kv.V = Vp; kv.max_pos = max_pos; kv.cur_pos = 0;
     gqa_attention(out, x, &ly, &kv, 0, pos, &c);
 }
+
+/* sample_logits (picchio.c:1540) with its globals (g_temperature, g_top_p,
+ * g_top_k, g_rep_penalty, g_history, g_history_len, g_rng) loaded from the
+ * arguments before the call and stored back after it. */
+REF_API int ref_sample_logits(float *logits, int vocab, float temperature, float top_p, int top_k,
+                              float rep, int *history, int *history_len, uint64_t *rng) {
+    g_temperature = temperature;
+    g_top_p = top_p;
+    g_top_k = top_k;
+    g_rep_penalty = rep;
+    g_history_len = *history_len;
+    memcpy(g_history, history, (size_t)g_history_len * sizeof(int));
+    g_rng = *rng;
+    const int id = sample_logits(logits, vocab);
+    *history_len = g_history_len;
+    memcpy(history, g_history, (size_t)g_history_len * sizeof(int));
+    *rng = g_rng;
+    return id;
+}

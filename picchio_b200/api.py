@@ -102,6 +102,10 @@ class ModelConfig:
 _lib = None
 
 
+class _Sampling(C.Structure):
+    _fields_ = [("temperature", C.c_float), ("top_p", C.c_float), ("top_k", C.c_int), ("rep_penalty", C.c_float)]
+
+
 def lib():
     """The loaded C library; raises if it has not been built."""
     global _lib
@@ -150,7 +154,18 @@ def lib():
         L.pc_profile_begin.argtypes = [vp]
         L.pc_profile_end.argtypes = [vp]
         L.pc_profile_get.argtypes = [vp, C.c_char_p, C.POINTER(C.c_double), ip]
-        for name in ("pc_generate", "pc_profile_begin", "pc_profile_end", "pc_profile_get"):
+        L.pc_set_sampling.argtypes = [vp, C.POINTER(_Sampling)]
+        L.pc_set_rng.argtypes = [vp, C.c_uint64]
+        L.pc_get_rng.argtypes = [vp, C.POINTER(C.c_uint64)]
+        L.pc_history_reset.argtypes = [vp]
+        L.pc_history_push.argtypes = [vp, ip, C.c_int]
+        L.pc_history_get.argtypes = [vp, ip, C.c_int, ip]
+        L.pc_sample.argtypes = [vp, vp, ip]
+        L.pc_expert_stats.argtypes = [vp, C.POINTER(C.c_uint64), C.POINTER(C.c_uint64), C.POINTER(C.c_uint64)]
+        L.pc_expert_stats.restype = st
+        for name in ("pc_generate", "pc_profile_begin", "pc_profile_end", "pc_profile_get", "pc_set_sampling",
+                     "pc_set_rng", "pc_get_rng", "pc_history_reset", "pc_history_push", "pc_history_get",
+                     "pc_sample"):
             getattr(L, name).restype = st
         for name in ("pc_init", "pc_init_synthetic", "pc_get_config", "pc_forward_token", "pc_prefill",
                      "pc_decode_batch", "pc_get_logits", "pc_moe_layer", "pc_moe_experts", "pc_set_trace",
@@ -184,12 +199,14 @@ class Model:
 
     def __init__(self, model_dir: str | None = None, *, cfg: ModelConfig | None = None, seed: int = 0,
                  ctx: int = 512, kv_bf16: bool = False, max_batch: int = 1, device: int = 0,
-                 use_graphs: bool = True, ep_rank: int = 0, ep_size: int = 1, nccl_id: bytes | None = None):
+                 use_graphs: bool = True, ep_rank: int = 0, ep_size: int = 1, nccl_id: bytes | None = None,
+                 expert_residency: int = 0, expert_cache_slots: int = 0):
         L = lib()
         o = _Opts()
         L.pc_default_opts(C.byref(o))
         o.device, o.ctx_len, o.kv_bf16, o.max_batch = device, ctx, int(kv_bf16), max_batch
         o.use_graphs, o.ep_rank, o.ep_size = int(use_graphs), ep_rank, ep_size
+        o.expert_residency, o.expert_cache_slots = int(expert_residency), int(expert_cache_slots)
         self._nid = C.create_string_buffer(nccl_id, 128) if nccl_id is not None else None
         o.nccl_id = C.cast(self._nid, C.c_void_p) if self._nid is not None else None
         h = C.c_void_p()
@@ -285,6 +302,54 @@ class Model:
         v = np.empty(self.config["vocab"], np.float32)
         _check(lib().pc_get_logits(self._h, row, v.ctypes.data_as(C.POINTER(C.c_float)), v.size))
         return v
+
+    def set_sampling(self, temperature: float | None = None, top_p: float = 1.0, top_k: int = 0,
+                     rep_penalty: float = 1.0):
+        """Device sample_logits for later single-sequence steps (None: argmax)."""
+        if temperature is None:
+            _check(lib().pc_set_sampling(self._h, None))
+            return
+        s = _Sampling(float(temperature), float(top_p), int(top_k), float(rep_penalty))
+        _check(lib().pc_set_sampling(self._h, C.byref(s)))
+
+    @property
+    def rng(self) -> int:
+        v = C.c_uint64(0)
+        _check(lib().pc_get_rng(self._h, C.byref(v)))
+        return int(v.value)
+
+    @rng.setter
+    def rng(self, state: int):
+        _check(lib().pc_set_rng(self._h, int(state)))
+
+    def history(self) -> list:
+        buf = np.zeros(4096, np.int32)
+        n = C.c_int(0)
+        _check(lib().pc_history_get(self._h, buf.ctypes.data_as(C.POINTER(C.c_int)), buf.size, C.byref(n)))
+        return buf[:n.value].tolist()
+
+    def history_reset(self):
+        _check(lib().pc_history_reset(self._h))
+
+    def history_push(self, ids):
+        a = np.ascontiguousarray(ids, np.int32)
+        _check(lib().pc_history_push(self._h, a.ctypes.data_as(C.POINTER(C.c_int)), a.size))
+
+    def sample(self, logits) -> int:
+        """One device draw from a [vocab] float32 CUDA tensor."""
+        out = C.c_int(0)
+        _check(lib().pc_sample(self._h, _dev_ptr(logits), C.byref(out)))
+        return int(out.value)
+
+    def expert_prefetch(self, layer: int, eids):
+        a = np.ascontiguousarray(eids, np.int32)
+        _check(lib().pc_expert_prefetch(self._h, int(layer), a.ctypes.data_as(C.POINTER(C.c_int)), a.size))
+
+    def expert_stats(self) -> dict:
+        """Streamed-residency counters: HBM-slot hits, host reads, bytes copied."""
+        h, m, b = C.c_uint64(), C.c_uint64(), C.c_uint64()
+        _check(lib().pc_expert_stats(self._h, C.byref(h), C.byref(m), C.byref(b)))
+        return {"hits": h.value, "misses": m.value, "bytes_h2d": b.value}
 
     def moe_forward(self, x, layer: int):
         """moe_forward for the rows of x ([M, D] float32 CUDA tensor)."""

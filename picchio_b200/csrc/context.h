@@ -10,6 +10,8 @@
 #include "../../include/picchio_b200.h"
 #include "decode.h"
 #include "layout.h"
+#include "residency.h"
+#include "sample.h"
 #include "tcgemm.h"
 
 namespace pc {
@@ -94,6 +96,8 @@ struct pc_ctx {
     unsigned long long *argmax = nullptr;
     int *err = nullptr;
     int max_logit_rows = 1;
+    pc::Sampler smp;  // device sample_logits (pc_set_sampling); off: argmax
+    pc::Residency res;  // streamed experts (opts.expert_residency == 1)
 
     std::map<uint64_t, pc::DenseJobs> dense_jobs;
     std::map<uint64_t, pc::StepGraph> graphs;

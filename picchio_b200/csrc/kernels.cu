@@ -360,8 +360,8 @@ __global__ void __launch_bounds__(256) router_kernel(const RouterParams r) {
         }
     }
     if (n == 0) return;
-    const int slot = r.slot_of ? r.slot_of[e] : e - r.e_lo;
-    const uint8_t *base = r.table + (int64_t)slot * r.stride;
+    if (r.used) r.used[e] = 1;
+    const uint8_t *base = r.emap ? r.emap[e] : r.table + (int64_t)(e - r.e_lo) * r.stride;
     int j = jstart[e], fill = 0;
     for (int p = 0; p < Ps && j < GEMV_MAX_JOBS; ++p) {
         if (ssel[p] != e) continue;

@@ -64,7 +64,10 @@ struct RouterParams {
     int64_t off_gu, off_dn, off_gu_rs, off_dn_rs, off_gu_b, off_dn_b;  // -1 = absent
     int gu_rt, dn_rt, gu_O, dn_O;
     int e_lo, e_hi;        // experts resident here (expert parallelism)
-    int *slot_of;          // optional [E] HBM slot of each expert (streamed residency) or null
+    // optional (streamed residency): [E] address of each expert's bytes, an
+    // HBM cache slot or its pinned host copy; null: table + (e - e_lo) * stride
+    const uint8_t *const *emap;
+    unsigned char *used;   // optional [E]: set to 1 for every expert a job reads
     GemvJob *jobs_gu, *jobs_dn;
     int per_job;           // (row, k) pairs per job, 1..GEMV_MAXR (0 = GEMV_MAXR)
     int *njobs;            // [2]: gate_up, down

@@ -560,6 +560,7 @@ pc_status load_model(pc_ctx *c, const std::string &dir) {
             PC_TRY(expert_matrix(db, l, e, "down_proj", D, k.intermediate, dn));
             if (!geom) {
                 PC_TRY(expert_geometry(c, gu.bs, dn.bs));
+                if (c->opts.expert_residency == 1) PC_TRY(res_init(c));
                 geom = true;
                 const int64_t raw = (int64_t)I2 * ((D + 1) / 2) + (int64_t)gu.s.size() * 4 +
                                     (int64_t)D * ((k.intermediate + 1) / 2) + (int64_t)dn.s.size() * 4 + 1024;
@@ -569,7 +570,8 @@ pc_status load_model(pc_ctx *c, const std::string &dir) {
                 return fail(PC_ERR_FORMAT, "experts with different INT4 group sizes in one model");
             if (!c->L[l].experts)
                 PC_TRY(dalloc(c, (size_t)(c->e_hi - c->e_lo) * c->eg.stride, (void **)&c->L[l].experts));
-            uint8_t *base = c->L[l].experts + (int64_t)(e - c->e_lo) * c->eg.stride;
+            // streamed residency: assembled in a staging expert, then stored on the host
+            uint8_t *base = c->res.on ? c->res.stage : c->L[l].experts + (int64_t)(e - c->e_lo) * c->eg.stride;
             TileDesc tg, td;
             expert_views(c, base, tg, td);
             uint8_t *d = (uint8_t *)dtmp;
@@ -588,8 +590,10 @@ pc_status load_model(pc_ctx *c, const std::string &dir) {
             PC_TRY(expert_bias(db, l, e, "down_proj_bias", E, D, bdn, &has));
             PC_CU(cudaMemcpy(base + c->eg.off_gu_b, bgu.data(), bgu.size() * 4, cudaMemcpyHostToDevice));
             PC_CU(cudaMemcpy(base + c->eg.off_dn_b, bdn.data(), bdn.size() * 4, cudaMemcpyHostToDevice));
+            if (c->res.on) PC_TRY(res_store(c, l, e));
         }
     }
+    if (c->res.on) PC_TRY(res_finish_load(c));
     if (dtmp) cudaFree(dtmp);
     (void)stage;
     return alloc_runtime(c);
@@ -662,10 +666,11 @@ pc_status synth_model(pc_ctx *c, uint64_t seed) {
         PC_TRY(vec(E, 0.0f, 0.01f, &ly.router_bias));
     }
     PC_TRY(expert_geometry(c, k.group_size, k.group_size));
+    if (c->opts.expert_residency == 1) PC_TRY(res_init(c));
     for (int l = 0; l < k.n_layers; ++l) {
-        PC_TRY(dalloc(c, (size_t)(c->e_hi - c->e_lo) * c->eg.stride, (void **)&c->L[l].experts));
+        if (!c->res.on) PC_TRY(dalloc(c, (size_t)(c->e_hi - c->e_lo) * c->eg.stride, (void **)&c->L[l].experts));
         for (int e = c->e_lo; e < c->e_hi; ++e) {
-            uint8_t *base = c->L[l].experts + (int64_t)(e - c->e_lo) * c->eg.stride;
+            uint8_t *base = c->res.on ? c->res.stage : c->L[l].experts + (int64_t)(e - c->e_lo) * c->eg.stride;
             TileDesc tg, td;
             expert_views(c, base, tg, td);
             PC_CU(gen_i4_rowmajor(tmp, tmps, I2, D, k.group_size, seed_of(seed, 1000 + l, e, 1), 0.02f, st));
@@ -674,9 +679,11 @@ pc_status synth_model(pc_ctx *c, uint64_t seed) {
             PC_CU(retile_t4(tmp, tmps, k.group_size, td, st));
             PC_CU(gen_f32(reinterpret_cast<float *>(base + c->eg.off_gu_b), I2, seed_of(seed, 1000 + l, e, 3), 0.0f, 0.01f, st));
             PC_CU(gen_f32(reinterpret_cast<float *>(base + c->eg.off_dn_b), D, seed_of(seed, 1000 + l, e, 4), 0.0f, 0.01f, st));
+            if (c->res.on) PC_TRY(res_store(c, l, e));
         }
         PC_CU(cudaStreamSynchronize(st));
     }
+    if (c->res.on) PC_TRY(res_finish_load(c));
     cudaFree(tmp);
     return alloc_runtime(c);
 }

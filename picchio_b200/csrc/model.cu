@@ -394,7 +394,8 @@ pc_status run_moe(pc_ctx *c, int l, const float *x, int M, const int *sel_in, co
     r.dn_O = c->eg.dn.O;
     r.e_lo = c->e_lo;
     r.e_hi = c->e_hi;
-    r.slot_of = nullptr;
+    r.emap = c->res.on ? c->res.emap + (size_t)l * k.n_experts : nullptr;
+    r.used = c->res.on ? c->res.used + (size_t)l * k.n_experts : nullptr;
     r.jobs_gu = c->jobs_gu;
     r.jobs_dn = c->jobs_dn;
     // Many rows but few pairs per expert (batched decode, ~2 per expert):
@@ -640,6 +641,11 @@ pc_status run_step(pc_ctx *c, int M, const int *seq, int lm_mode, int nsplit_ful
     trace_row(c, "logits", c->logits + (size_t)(nlog - 1) * k.vocab, k.vocab);
     PC_CU(launch_argmax_finish(c->argmax, nlog, c->d_next, feedback ? c->d_tok : nullptr, c->st));
     ++c->launches;
+    if (c->smp.on && nlog == 1) {  // sample_logits on the device: overwrites the argmax id
+        int n = 0;
+        PC_CU(sampler_launch(c->smp, c->logits, c->d_next, feedback ? c->d_tok : nullptr, c->err, c->st, n));
+        c->launches += n;
+    }
     if (feedback) {  // on-device loop: record the id, advance the position
         PC_CU(launch_gen_advance(c->d_next, c->d_pos, c->d_gen, c->d_step, c->st));
     }
@@ -656,12 +662,20 @@ int split_bucket(const pc_ctx *c, int max_pos) {
 
 pc_status check_err(pc_ctx *c) {
     if (*c->h_err) {
+        const int v = *c->h_err;
         *c->h_err = 0;
         cudaMemsetAsync(c->err, 0, 4, c->st);
+        if (v == SAMPLE_ERR_CANDIDATES)
+            return fail(PC_ERR_RANGE, "sampling: more than " + std::to_string(SAMPLE_SORT_CAP) +
+                                          " top-p candidates (values tied at the top-k threshold)");
         return fail(PC_ERR_TIMEOUT, "a device-side bounded wait gave up");
     }
     return PC_OK;
 }
+
+// Graph-key bits of the sampler configuration (its launches are part of the
+// captured step).
+uint64_t sampler_key(const pc_ctx *c) { return c->smp.on ? (c->smp.big ? 2ull : 1ull) << 56 : 0ull; }
 
 // Runs `body` on the context stream: captured once into a CUDA graph under
 // `key` and replayed afterwards, unless graphs are off or the step is traced
@@ -718,6 +732,7 @@ pc_status run_graph(pc_ctx *c, uint64_t key, F &&body) {
 pc_status decode_setup(pc_ctx *c) {
     if (c->dec_state != 0) return PC_OK;
     c->dec_state = -1;
+    if (c->res.on) return PC_OK;  // the persistent kernel indexes the HBM expert table
     const char *env = getenv("PICCHIO_PERSISTENT");
     if (!env || env[0] != '1') return PC_OK;
     const pc_model_cfg &k = c->cfg;
@@ -853,7 +868,7 @@ pc_status decode_persistent(pc_ctx *c, int nsteps, int *gen) {
 // Decode-shaped step (tokens/positions in h_tok/h_pos, M rows, KV slot =
 // row for batches, 0 for a single sequence): graph replay when enabled.
 pc_status decode_step(pc_ctx *c, int M, int *next) {
-    if (M == 1 && !c->trace && !c->prof) {
+    if (M == 1 && !c->trace && !c->prof && !c->smp.on) {
         PC_TRY(decode_setup(c));
         if (c->dec_state == 1) {
             PC_CU(cudaMemcpyAsync(c->d_tok, c->h_tok, 4, cudaMemcpyHostToDevice, c->st));
@@ -881,9 +896,10 @@ pc_status decode_step(pc_ctx *c, int M, int *next) {
         PC_CU(cudaMemcpyAsync(c->h_err, c->err, 4, cudaMemcpyDeviceToHost, c->st));
         return PC_OK;
     };
-    PC_TRY(run_graph(c, ((uint64_t)M << 20) | (uint64_t)ns, body));
+    PC_TRY(run_graph(c, ((uint64_t)M << 20) | (uint64_t)ns | sampler_key(c), body));
     PC_CU(cudaStreamSynchronize(c->st));
     PC_TRY(check_err(c));
+    PC_TRY(res_after_step(c));
     for (int i = 0; i < M; ++i) next[i] = c->h_next[i];
     return PC_OK;
 }
@@ -897,7 +913,7 @@ pc_status generate(pc_ctx *c, int tok, int pos, int n, int *out, float *device_m
     PC_TRY(dense_jobs(c, 1, 0, &dj));
     auto body = [&]() -> pc_status { return run_step(c, 1, c->d_seq_rows, 0, ns, dj, true); };
     if (!c->trace && !c->prof) PC_TRY(decode_setup(c));
-    const bool persistent = c->dec_state == 1 && !c->trace && !c->prof;
+    const bool persistent = c->dec_state == 1 && !c->trace && !c->prof && !c->smp.on;
     c->h_tok[0] = tok;
     c->h_pos[0] = pos;
     PC_CU(cudaMemcpyAsync(c->d_tok, c->h_tok, 4, cudaMemcpyHostToDevice, c->st));
@@ -910,7 +926,7 @@ pc_status generate(pc_ctx *c, int tok, int pos, int n, int *out, float *device_m
     if (persistent) {
         PC_TRY(decode_persistent(c, n, c->d_gen));
     } else {
-        for (int i = 0; i < n; ++i) PC_TRY(run_graph(c, (1ull << 62) | (uint64_t)ns, body));
+        for (int i = 0; i < n; ++i) PC_TRY(run_graph(c, (1ull << 62) | (uint64_t)ns | sampler_key(c), body));
     }
     PC_CU(cudaEventRecord(e1, c->st));
     PC_CU(cudaMemcpyAsync(out, c->d_gen, (size_t)n * 4, cudaMemcpyDeviceToHost, c->st));
@@ -921,7 +937,8 @@ pc_status generate(pc_ctx *c, int tok, int pos, int n, int *out, float *device_m
     cudaEventDestroy(e0);
     cudaEventDestroy(e1);
     if (device_ms) *device_ms = ms;
-    return check_err(c);
+    PC_TRY(check_err(c));
+    return res_after_step(c);
 }
 
 pc_status check_ctx(pc_ctx *c) {
@@ -937,6 +954,10 @@ pc_status make_ctx(const pc_opts *opts, pc_ctx **out) {
     pc_ctx *c = new pc_ctx();
     if (opts) c->opts = *opts;
     else pc_default_opts(&c->opts);
+    if (c->opts.expert_residency != 0 && c->opts.expert_residency != 1) {
+        delete c;
+        return fail(PC_ERR_INVALID_ARG, "expert_residency must be 0 (HBM table) or 1 (pinned host + HBM slots)");
+    }
     c->dev = c->opts.device;
     pc_status s = configure_device(c);
     if (s != PC_OK) { delete c; return s; }
@@ -954,8 +975,8 @@ pc_status make_ctx(const pc_opts *opts, pc_ctx **out) {
 pc_status tc_setup(pc_ctx *c) {
     const char *v = getenv("PICCHIO_TC");
     if ((v && v[0] == '0') || !tc_driver_ready() || c->L.empty()) return PC_OK;
-    // expert GEMMs (INT4 experts)
-    if (c->eg.gu.fmt == TF_T4 && c->eg.dn.fmt == TF_T4 && c->eg.gu.blk_bytes <= 768 && c->eg.dn.blk_bytes <= 768 &&
+    // expert GEMMs (INT4 experts resident in HBM)
+    if (!c->res.on && c->eg.gu.fmt == TF_T4 && c->eg.dn.fmt == TF_T4 && c->eg.gu.blk_bytes <= 768 && c->eg.dn.blk_bytes <= 768 &&
         c->eg.gu.Ip % 64 == 0 && c->eg.dn.Ip % 64 == 0) {
         const int pairs = c->maxm * c->cfg.topk;
         PC_TRY(dalloc(c, (size_t)(c->cfg.n_experts + 1) * 4, (void **)&c->pair_start));
@@ -1100,6 +1121,8 @@ void pc_free(pc_ctx *c) {
     for (auto &g : c->graphs) cudaGraphExecDestroy(g.second.exec);
     c->graphs.clear();
     ep_destroy(c);
+    sampler_free(c->smp);
+    res_free(c);
     for (void *p : c->allocs) cudaFree(p);
     if (c->pinned) cudaFreeHost(c->pinned);
     if (c->st) cudaStreamDestroy(c->st);
@@ -1147,11 +1170,14 @@ pc_status pc_prefill(pc_ctx *c, const int *ids, int n, int pos_base, int *next_t
         for (int i = 0; i < m; ++i) { tok[i] = ids[off + i]; ps[i] = pos_base + off + i; }
         PC_CU(cudaMemcpyAsync(c->d_tok, tok.data(), (size_t)m * 4, cudaMemcpyHostToDevice, c->st));
         PC_CU(cudaMemcpyAsync(c->d_pos, ps.data(), (size_t)m * 4, cudaMemcpyHostToDevice, c->st));
-        const bool last = off + m >= n;
+        // with device sampling every block draws, as every forward_prefill
+        // block of the reference does (picchio.c:1920-1926, 1970-1973)
+        const bool lm = off + m >= n || c->smp.on;
         DenseJobs *dj = nullptr;
-        PC_TRY(dense_jobs(c, m, last ? 1 : 2, &dj));
-        PC_TRY(run_step(c, m, c->d_seq_zero, last ? 1 : 2, split_bucket(c, ps[m - 1]), dj));
+        PC_TRY(dense_jobs(c, m, lm ? 1 : 2, &dj));
+        PC_TRY(run_step(c, m, c->d_seq_zero, lm ? 1 : 2, split_bucket(c, ps[m - 1]), dj));
         PC_CU(cudaStreamSynchronize(c->st));
+        PC_TRY(res_after_step(c));
     }
     PC_CU(cudaMemcpy(c->h_next, c->d_next, 4, cudaMemcpyDeviceToHost));
     PC_CU(cudaMemcpy(c->h_err, c->err, 4, cudaMemcpyDeviceToHost));
@@ -1165,6 +1191,103 @@ pc_status pc_get_logits(pc_ctx *c, int row, float *logits, int n) {
     if (!logits || row < 0 || row >= c->max_logit_rows || n > c->cfg.vocab) return fail(PC_ERR_INVALID_ARG, "bad logits request");
     PC_CU(cudaStreamSynchronize(c->st));
     PC_CU(cudaMemcpy(logits, c->logits + (size_t)row * c->cfg.vocab, (size_t)n * 4, cudaMemcpyDeviceToHost));
+    return PC_OK;
+}
+
+pc_status pc_set_sampling(pc_ctx *c, const pc_sampling *s) {
+    PC_TRY(check_ctx(c));
+    if (!s) {
+        c->smp.on = false;
+        return PC_OK;
+    }
+    if (!(s->temperature >= 0.0f) || !(s->top_p == s->top_p) || !(s->rep_penalty == s->rep_penalty))
+        return fail(PC_ERR_INVALID_ARG, "sampling settings must be numbers, temperature >= 0");
+    const int V = c->cfg.vocab;
+    PC_CU(sampler_init(c->smp, V));
+    SampleParams p{};
+    p.temperature = s->temperature;
+    p.top_p = s->top_p;
+    p.rep = s->rep_penalty;
+    p.inv_temp = s->temperature < 1e-6f ? 1.0f : 1.0f / s->temperature;  // picchio.c:1564
+    p.top_k = s->top_k;
+    PC_CU(cudaMemcpyAsync(&c->smp.state->p, &p, sizeof p, cudaMemcpyHostToDevice, c->st));
+    PC_CU(cudaStreamSynchronize(c->st));
+    const bool top_p = s->top_p < 1.0f && s->top_p > 0.0f;
+    const bool small_k = s->top_k > 0 && s->top_k < V && s->top_k <= SAMPLE_TOPK_SMALL;
+    c->smp.big = top_p && !small_k;
+    c->smp.on = true;
+    return PC_OK;
+}
+
+pc_status pc_set_rng(pc_ctx *c, uint64_t state) {
+    PC_TRY(check_ctx(c));
+    PC_CU(sampler_init(c->smp, c->cfg.vocab));
+    const unsigned long long v = state;
+    PC_CU(cudaMemcpyAsync(&c->smp.state->rng, &v, sizeof v, cudaMemcpyHostToDevice, c->st));
+    PC_CU(cudaStreamSynchronize(c->st));
+    return PC_OK;
+}
+
+pc_status pc_get_rng(pc_ctx *c, uint64_t *state) {
+    PC_TRY(check_ctx(c));
+    if (!state) return fail(PC_ERR_INVALID_ARG, "null state");
+    PC_CU(sampler_init(c->smp, c->cfg.vocab));
+    unsigned long long v = 0;
+    PC_CU(cudaStreamSynchronize(c->st));
+    PC_CU(cudaMemcpy(&v, &c->smp.state->rng, sizeof v, cudaMemcpyDeviceToHost));
+    *state = v;
+    return PC_OK;
+}
+
+pc_status pc_history_reset(pc_ctx *c) {
+    PC_TRY(check_ctx(c));
+    PC_CU(sampler_init(c->smp, c->cfg.vocab));
+    PC_CU(cudaMemsetAsync(&c->smp.state->hist_len, 0, sizeof(int), c->st));
+    PC_CU(cudaStreamSynchronize(c->st));
+    return PC_OK;
+}
+
+pc_status pc_history_push(pc_ctx *c, const int *ids, int n) {
+    PC_TRY(check_ctx(c));
+    if (n < 0 || (n > 0 && !ids)) return fail(PC_ERR_INVALID_ARG, "bad history ids");
+    PC_CU(sampler_init(c->smp, c->cfg.vocab));
+    PC_CU(cudaStreamSynchronize(c->st));
+    int len = 0;
+    PC_CU(cudaMemcpy(&len, &c->smp.state->hist_len, sizeof len, cudaMemcpyDeviceToHost));
+    std::vector<int> keep;  // ids outside the vocabulary take no slot (picchio.c:1964-1966)
+    for (int i = 0; i < n && len + (int)keep.size() < SAMPLE_HIST_CAP; ++i)
+        if (ids[i] >= 0 && ids[i] < c->cfg.vocab) keep.push_back(ids[i]);
+    if (keep.empty()) return PC_OK;
+    PC_CU(cudaMemcpy(c->smp.hist + len, keep.data(), keep.size() * sizeof(int), cudaMemcpyHostToDevice));
+    len += (int)keep.size();
+    PC_CU(cudaMemcpy(&c->smp.state->hist_len, &len, sizeof len, cudaMemcpyHostToDevice));
+    return PC_OK;
+}
+
+pc_status pc_history_get(pc_ctx *c, int *ids, int cap, int *n) {
+    PC_TRY(check_ctx(c));
+    if (!n || cap < 0 || (cap > 0 && !ids)) return fail(PC_ERR_INVALID_ARG, "bad history request");
+    PC_CU(sampler_init(c->smp, c->cfg.vocab));
+    PC_CU(cudaStreamSynchronize(c->st));
+    int len = 0;
+    PC_CU(cudaMemcpy(&len, &c->smp.state->hist_len, sizeof len, cudaMemcpyDeviceToHost));
+    *n = len;
+    if (cap > 0 && len > 0) PC_CU(cudaMemcpy(ids, c->smp.hist, (size_t)std::min(cap, len) * sizeof(int), cudaMemcpyDeviceToHost));
+    return PC_OK;
+}
+
+pc_status pc_sample(pc_ctx *c, const float *logits_dev, int *id) {
+    PC_TRY(check_ctx(c));
+    if (!logits_dev || !id) return fail(PC_ERR_INVALID_ARG, "null argument");
+    if (!c->smp.on) return fail(PC_ERR_STATE, "no sampling settings (pc_set_sampling)");
+    int launches = 0;
+    PC_CU(sampler_launch(c->smp, logits_dev, c->d_next, nullptr, c->err, c->st, launches));
+    c->launches += launches;
+    PC_CU(cudaMemcpyAsync(c->h_next, c->d_next, 4, cudaMemcpyDeviceToHost, c->st));
+    PC_CU(cudaMemcpyAsync(c->h_err, c->err, 4, cudaMemcpyDeviceToHost, c->st));
+    PC_CU(cudaStreamSynchronize(c->st));
+    PC_TRY(check_err(c));
+    *id = c->h_next[0];
     return PC_OK;
 }
 
@@ -1192,7 +1315,8 @@ pc_status pc_moe_layer(pc_ctx *c, int layer, const float *x_dev, float *out_dev,
     PC_TRY(run_moe_rows(c, layer, x_dev, M, nullptr, nullptr, out_dev));
     PC_CU(cudaMemcpyAsync(c->h_err, c->err, 4, cudaMemcpyDeviceToHost, c->st));
     PC_CU(cudaStreamSynchronize(c->st));
-    return check_err(c);
+    PC_TRY(check_err(c));
+    return res_after_step(c);
 }
 
 pc_status pc_moe_experts(pc_ctx *c, int layer, const float *x_dev, const int *sel_dev, const float *w_dev, int M,
@@ -1204,7 +1328,8 @@ pc_status pc_moe_experts(pc_ctx *c, int layer, const float *x_dev, const int *se
     PC_TRY(run_moe_rows(c, layer, x_dev, M, sel_dev, w_dev, out_dev));
     PC_CU(cudaMemcpyAsync(c->h_err, c->err, 4, cudaMemcpyDeviceToHost, c->st));
     PC_CU(cudaStreamSynchronize(c->st));
-    return check_err(c);
+    PC_TRY(check_err(c));
+    return res_after_step(c);
 }
 
 pc_status pc_set_trace(pc_ctx *c, int on) {
@@ -1251,7 +1376,15 @@ pc_status pc_expert_prefetch(pc_ctx *c, int layer, const int *eids, int n) {
     if (!c) return fail(PC_ERR_INVALID_ARG, "null context");
     if (layer < 0 || layer >= c->cfg.n_layers || n < 0 || (n > 0 && !eids))
         return fail(PC_ERR_INVALID_ARG, "bad pc_expert_prefetch arguments");
-    // Every expert is resident in HBM in this build: nothing to fetch.
+    PC_TRY(check_ctx(c));
+    return res_prefetch(c, layer, eids, n);  // no-op when the whole table is in HBM
+}
+
+pc_status pc_expert_stats(pc_ctx *c, uint64_t *hits, uint64_t *misses, uint64_t *bytes_h2d) {
+    if (!c) return fail(PC_ERR_INVALID_ARG, "null context");
+    if (hits) *hits = c->res.hits;
+    if (misses) *misses = c->res.misses;
+    if (bytes_h2d) *bytes_h2d = c->res.bytes;
     return PC_OK;
 }
 

@@ -8,16 +8,16 @@
  * the CUDA ordinal.  There is no tokenizer here: prompts are token ids, as
  * the reference takes them when it has no tokenizer.json.
  *
- * Greedy decoding (TEMPERATURE=0) takes the next id from the device argmax;
- * other settings copy the logits back and sample on the host with the
- * reference's procedure (picchio.c:1520-1649).
+ * Greedy decoding without a repetition penalty takes the next id from the
+ * device argmax; any other setting draws it on the device (pc_set_sampling:
+ * the reference's sample_logits, picchio.c:1520-1649, with the generator
+ * state and the repetition history kept in device memory).
  */
 #include <limits.h>
 #include <stdint.h>
 #include <stdio.h>
 #include <stdlib.h>
 #include <string.h>
-#include <math.h>
 #include <time.h>
 
 #include "picchio_b200.h"
@@ -25,101 +25,24 @@
 #define TOK_RETURN 200002
 #define TOK_CALL 200012
 
+/* the reference's defaults (picchio.c:1510-1520) */
 static float g_temperature = 1.0f, g_top_p = 0.95f, g_rep = 1.1f;
 static int g_top_k = 50;
-static int g_history[4096];
-static int g_history_len = 0;
-static uint64_t g_rng = 1234567890123456789ULL;
+static uint64_t g_seed = 1234567890123456789ULL;
 
-static float rng_float(void) { /* xorshift64, picchio.c:1521-1526 */
-    g_rng ^= g_rng << 13;
-    g_rng ^= g_rng >> 7;
-    g_rng ^= g_rng << 17;
-    return (float)(g_rng >> 33) / (float)(1ULL << 31);
-}
-
-typedef struct { float v; int i; } IV;
-static int cmp_iv(const void *a, const void *b) {
-    float x = ((const IV *)a)->v, y = ((const IV *)b)->v;
-    return (x < y) - (x > y);
-}
-static int cmp_f(const void *a, const void *b) {
-    float x = *(const float *)a, y = *(const float *)b;
-    return (x < y) - (x > y);
-}
-
-/* sample_logits (picchio.c:1540-1649) for TEMPERATURE > 0. */
-static int sample_host(float *lg, int V) {
-    if (g_rep > 1.0f)
-        for (int i = 0; i < g_history_len; i++) {
-            int t = g_history[i];
-            if (t >= 0 && t < V) lg[t] = lg[t] > 0 ? lg[t] / g_rep : lg[t] * g_rep;
-        }
-    if (g_temperature < 1e-6f) {
-        int best = 0;
-        for (int i = 1; i < V; i++) if (lg[i] > lg[best]) best = i;
-        if (g_history_len < 4096) g_history[g_history_len++] = best;
-        return best;
-    }
-    float inv = 1.0f / g_temperature;
-    for (int i = 0; i < V; i++) lg[i] *= inv;
-    if (g_top_k > 0 && g_top_k < V) {
-        float *s = (float *)malloc((size_t)V * sizeof(float));
-        if (s) {
-            memcpy(s, lg, (size_t)V * sizeof(float));
-            qsort(s, V, sizeof(float), cmp_f);
-            float th = s[g_top_k - 1];
-            free(s);
-            for (int i = 0; i < V; i++) if (lg[i] < th) lg[i] = -1e30f;
-        }
-    }
-    float mx = -1e30f;
-    for (int i = 0; i < V; i++) if (lg[i] > mx) mx = lg[i];
-    float sum = 0;
-    for (int i = 0; i < V; i++) { lg[i] = expf(lg[i] - mx); sum += lg[i]; }
-    for (int i = 0; i < V; i++) lg[i] /= sum;
-    if (g_top_p < 1.0f && g_top_p > 0.0f) {
-        int n = 0;
-        for (int i = 0; i < V; i++) if (lg[i] > 1e-10f) n++;
-        if (n > 1) {
-            IV *so = (IV *)malloc((size_t)n * sizeof(IV));
-            int k = 0;
-            for (int i = 0; i < V; i++) if (lg[i] > 1e-10f) { so[k].v = lg[i]; so[k].i = i; k++; }
-            qsort(so, n, sizeof(IV), cmp_iv);
-            float cum = 0;
-            int cut = n;
-            for (int i = 0; i < n; i++) { cum += so[i].v; if (cum >= g_top_p) { cut = i + 1; break; } }
-            for (int i = cut; i < n; i++) lg[so[i].i] = 0.0f;
-            sum = 0;
-            for (int i = 0; i < V; i++) sum += lg[i];
-            if (sum > 0) for (int i = 0; i < V; i++) lg[i] /= sum;
-            free(so);
-        }
-    }
-    float r = rng_float(), cum = 0;
-    for (int i = 0; i < V; i++) {
-        cum += lg[i];
-        if (cum >= r) { if (g_history_len < 4096) g_history[g_history_len++] = i; return i; }
-    }
-    for (int i = V - 1; i >= 0; i--)
-        if (lg[i] > 0) { if (g_history_len < 4096) g_history[g_history_len++] = i; return i; }
-    return 0;
-}
-
+/* Device sampling is needed unless decoding is greedy without a penalty
+ * (then sample_logits is the plain argmax, picchio.c:1555-1560, and the
+ * history it records is never read). */
 static pc_model_cfg g_cfg;
-static float *g_logits = NULL;
 
-static int need_host_sampling(void) { return !(g_temperature < 1e-6f) || g_rep > 1.0f; }
-
-/* Picks the next id after a forward: device argmax when greedy without a
- * repetition penalty, else the host sampler on the copied logits. */
-static int choose(pc_ctx *ctx, int device_pick) {
-    if (!need_host_sampling()) {
-        if (g_history_len < 4096) g_history[g_history_len++] = device_pick;
-        return device_pick;
-    }
-    if (pc_get_logits(ctx, 0, g_logits, g_cfg.vocab) != PC_OK) return device_pick;
-    return sample_host(g_logits, g_cfg.vocab);
+static pc_status apply_sampling(pc_ctx *ctx) {
+    if (g_temperature < 1e-6f && !(g_rep > 1.0f)) return pc_set_sampling(ctx, NULL);
+    pc_sampling s;
+    s.temperature = g_temperature;
+    s.top_p = g_top_p;
+    s.top_k = g_top_k;
+    s.rep_penalty = g_rep;
+    return pc_set_sampling(ctx, &s);
 }
 
 static int die(const char *what, pc_status s) {
@@ -159,7 +82,8 @@ static int service(pc_ctx *ctx, int cap) {
         if (!strcmp(cmd, "SHUTDOWN")) break;
         if (!strcmp(cmd, "RESET")) {
             pos = 0;
-            g_history_len = 0;
+            pc_status rs = pc_history_reset(ctx);
+            if (rs != PC_OK) return die("history reset", rs);
             printf("DONE RESET 0 0\n");
             fflush(stdout);
             continue;
@@ -179,6 +103,8 @@ static int service(pc_ctx *ctx, int cap) {
         g_temperature = t_temp;
         g_top_p = t_topp;
         g_top_k = (int)t_topk;
+        pc_status ss = apply_sampling(ctx);
+        if (ss != PC_OK) return die("sampling settings", ss);
         if (max_new < 0 || keep < 0 || keep > pos || n_ids <= 0 || keep + n_ids > cap || n_ids > cap) {
             printf("ERROR BAD_RANGE 0 keep/n_ids out of bounds (pos=%d cap=%d)\n", pos, cap);
             fflush(stdout);
@@ -196,10 +122,12 @@ static int service(pc_ctx *ctx, int cap) {
         if (!valid) { free(ids); printf("ERROR BAD_TOKEN 0 ID out of vocabulary\n"); fflush(stdout); continue; }
         pos = (int)keep;  /* prefix reuse: later positions are overwritten */
         int next;
-        pc_status s = pc_prefill(ctx, ids, (int)n_ids, pos, &next);
+        pc_status s = PC_OK;
+        /* prefill_tokens seeds the history with a multi-token prompt (picchio.c:1963-1967) */
+        if (g_rep > 1.0f && n_ids > 1) s = pc_history_push(ctx, ids, (int)n_ids);
+        if (s == PC_OK) s = pc_prefill(ctx, ids, (int)n_ids, pos, &next);
         free(ids);
         if (s != PC_OK) return die("prefill", s);
-        next = choose(ctx, next);
         pos += (int)n_ids;
         const char *reason = "MAX_TOKENS";
         int produced = 0, tok = next;
@@ -212,7 +140,6 @@ static int service(pc_ctx *ctx, int cap) {
             int following;
             s = pc_forward_token(ctx, tok, pos, &following);
             if (s != PC_OK) return die("forward", s);
-            following = choose(ctx, following);
             pos++;
             if (tok == TOK_RETURN) { reason = "RETURN"; break; }
             if (tok == TOK_CALL) { reason = "CALL"; break; }
@@ -249,15 +176,16 @@ int main(int argc, char **argv) {
     if ((v = getenv("TOPP"))) g_top_p = (float)atof(v);
     if ((v = getenv("TOPK"))) g_top_k = atoi(v);
     if ((v = getenv("REP"))) g_rep = (float)atof(v);
-    if ((v = getenv("SEED"))) g_rng = (uint64_t)atoll(v);
-    else g_rng = (uint64_t)time(NULL);
+    if ((v = getenv("SEED"))) g_seed = (uint64_t)atoll(v);
+    else g_seed = (uint64_t)time(NULL);
 
     pc_ctx *ctx = NULL;
     double t0 = now_s();
     pc_status s = pc_init(model, &o, &ctx);
     if (s != PC_OK) return die("pc_init", s);
     pc_get_config(ctx, &g_cfg);
-    g_logits = (float *)malloc((size_t)g_cfg.vocab * sizeof(float));
+    if ((s = pc_set_rng(ctx, g_seed)) != PC_OK || (s = apply_sampling(ctx)) != PC_OK)
+        return die("sampling setup", s);
     fprintf(stderr, "loaded %s in %.1f s: D=%d L=%d E=%d top%d vocab=%d ctx=%d\n", model, now_s() - t0,
             g_cfg.hidden, g_cfg.n_layers, g_cfg.n_experts, g_cfg.topk, g_cfg.vocab, o.ctx_len);
 
@@ -295,15 +223,14 @@ int main(int argc, char **argv) {
             pc_free(ctx);
             return 1;
         }
-    if (g_rep > 1.0f)
-        for (int i = 0; i < n_prompt && g_history_len < 4096; i++) g_history[g_history_len++] = prompt[i];
+    if (g_rep > 1.0f && n_prompt > 1 && (s = pc_history_push(ctx, prompt, n_prompt)) != PC_OK)  /* picchio.c:1963-1967 */
+        return die("history", s);
     int output_ids = (v = getenv("OUTPUT")) && !strcmp(v, "ids");
 
     double tp = now_s();
     int tok;
     s = pc_prefill(ctx, prompt, n_prompt, 0, &tok);
     if (s != PC_OK) return die("prefill", s);
-    tok = choose(ctx, tok);
     fprintf(stderr, "prefill %d tokens in %.3f s\n", n_prompt, now_s() - tp);
     double tg = now_s();
     int pos = n_prompt, emitted = 0;
@@ -315,7 +242,7 @@ int main(int argc, char **argv) {
         int next;
         s = pc_forward_token(ctx, tok, pos, &next);
         if (s != PC_OK) return die("forward", s);
-        tok = choose(ctx, next);
+        tok = next;
         pos++;
         emitted++;
     }
@@ -323,7 +250,6 @@ int main(int argc, char **argv) {
     double dt = now_s() - tg;
     if (emitted > 0) fprintf(stderr, "generated %d tokens in %.3f s (%.1f tok/s)\n", emitted, dt, emitted / dt);
     free(prompt);
-    free(g_logits);
     pc_free(ctx);
     return 0;
 }

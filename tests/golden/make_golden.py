@@ -77,6 +77,32 @@ def make_variant(name, opts, seed=1234, prompt_seed=7):
     print(name, "ids", ids_batched[:12], "...", "batched==sequential:", ids_batched == ids_seq)
 
 
+# Reference runs with its sampler on (sample_logits, picchio.c:1540-1649):
+# the default settings (top-k 50, the in-block candidate sort on the device)
+# and a top-k-free nucleus (the large candidate sort).
+SAMPLED = [
+    {"TEMPERATURE": "1.0", "TOPP": "0.95", "TOPK": "50", "REP": "1.1", "SEED": "4242"},
+    {"TEMPERATURE": "0.8", "TOPP": "0.9", "TOPK": "0", "REP": "1.0", "SEED": "77"},
+]
+SAMPLED_STEPS = 48
+
+
+def add_sampled(name):
+    """Adds the reference's sampled ids (key "sampled") to <name>.json."""
+    path = os.path.join(HERE, f"{name}.json")
+    with open(path) as f:
+        meta = json.load(f)
+    with tempfile.TemporaryDirectory() as d:
+        make_model(d, SynthConfig(**meta["options"]), meta["seed"])
+        pf = os.path.join(d, "prompt.txt")
+        with open(pf, "w") as f:
+            f.write(" ".join(map(str, meta["prompt"])))
+        meta["sampled"] = [{"env": env, "ids": run_ref(d, pf, SAMPLED_STEPS, env)} for env in SAMPLED]
+    with open(path, "w") as f:
+        json.dump(meta, f, indent=1)
+    print(name, "sampled", [r["ids"][:8] for r in meta["sampled"]])
+
+
 def make_kernels():
     import ctypes as C
     R = O.ref_lib()
@@ -110,4 +136,5 @@ if __name__ == "__main__":
     O.build(ref=True)
     for n, o in VARIANTS.items():
         make_variant(n, o)
+    add_sampled("tiny_gs32_i8")
     make_kernels()

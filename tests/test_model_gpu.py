@@ -331,3 +331,41 @@ def test_batched_rows_attention_matches_single_row():
         la = a.logits(0)
     assert nxt[0] == t
     assert rel_l2(lb, la) < 2e-3
+
+
+@pytest.mark.parametrize("slots", [2, 8])
+def test_streamed_expert_residency_matches_reference(tmp_path, slots):
+    """expert_residency = 1: experts in pinned host memory, `slots` per layer
+    in HBM (8 = the whole layer).  Greedy ids equal the reference's; every
+    expert read is counted as a slot hit or a host read, and with two slots
+    of eight both happen."""
+    from picchio_b200 import Model
+    m = meta("tiny_gs32_i8")
+    d = str(tmp_path)
+    make_model(d, SynthConfig(**m["options"]), m["seed"])
+    with Model(d, ctx=m["ctx"], expert_residency=1, expert_cache_slots=slots) as model:
+        ids = model.generate(m["prompt"], 48)
+        st = model.expert_stats()
+        E, L = model.config["n_experts"], model.config["n_layers"]
+    assert ids == m["ids_batched"][:48]
+    assert st["misses"] > 0 and st["hits"] > 0
+    assert st["bytes_h2d"] > 0
+    if slots >= E:  # everything fits: each (layer, expert) is read from the host at most once
+        assert st["misses"] <= L * E
+
+
+def test_expert_prefetch_makes_later_reads_hits(tmp_path):
+    from picchio_b200 import Model
+    m = meta("tiny_gs32_i8")
+    d = str(tmp_path)
+    make_model(d, SynthConfig(**m["options"]), m["seed"])
+    with Model(d, ctx=m["ctx"], expert_residency=1, expert_cache_slots=8) as model:
+        E, L = model.config["n_experts"], model.config["n_layers"]
+        for layer in range(L):
+            model.expert_prefetch(layer, list(range(E)))
+        st0 = model.expert_stats()
+        ids = model.generate(m["prompt"], 16)
+        st1 = model.expert_stats()
+    assert ids == m["ids_batched"][:16]
+    assert st0["misses"] == 0 and st0["bytes_h2d"] > 0
+    assert st1["misses"] == 0 and st1["hits"] > 0

@@ -150,3 +150,34 @@ def test_oracle_matches_compiled_reference_random(shape):
     yn = np.empty(I, np.float32)
     R.ref_rmsnorm(yn.ctypes.data_as(fp), xx.ctypes.data_as(fp), ww.ctypes.data_as(fp), I, 1e-5)
     assert np.array_equal(bits(O.rmsnorm(xx, ww, 1e-5)), bits(yn))
+
+
+SAMPLER_SETTINGS = [
+    # (temperature, top_p, top_k, rep): the reference defaults, a top-k-free
+    # nucleus, no truncation at all, penalized greedy, a large top-k
+    (1.0, 0.95, 50, 1.1),
+    (0.7, 0.9, 0, 1.0),
+    (1.3, 1.0, 0, 1.0),
+    (0.0, 1.0, 0, 1.3),
+    (1.0, 0.5, 3000, 1.2),
+]
+
+
+@pytest.mark.skipif(O.ref_lib() is None or not hasattr(O.ref_lib(), "ref_sample_logits"),
+                    reason="reference not built here (oracle/_ref)")
+@pytest.mark.parametrize("V", [1024, 201088])
+@pytest.mark.parametrize("setting", SAMPLER_SETTINGS)
+def test_sampler_restatement_matches_reference(V, setting):
+    """or_sample against the reference's own sample_logits over a chain of
+    draws: same ids, same logits bits afterwards, same history and generator."""
+    T, tp, tk, rep = setting
+    rng = np.random.default_rng(V + tk)
+    so = O.SamplerState(987654321, rng.integers(0, V, 200))
+    sr = so.copy()
+    for _ in range(8 if V > 4096 else 24):
+        lg = (rng.standard_normal(V) * 2.5).astype(np.float32)
+        a, la = O.sample(lg, T, tp, tk, rep, so)
+        b, lb = O.ref_sample(lg, T, tp, tk, rep, sr)
+        assert a == b
+        assert np.array_equal(la.view(np.uint32), lb.view(np.uint32))
+        assert so.rng == sr.rng and so.history == sr.history
