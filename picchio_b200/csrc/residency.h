@@ -7,10 +7,16 @@
 // keeps `expert_cache_slots` experts in HBM slots.  The router reads each
 // expert's address from a device map (slot or host copy) and flags the
 // experts its jobs read, so a step never waits for the host: a miss is read
-// over the host link inside the step.  After the step the host moves the
-// flagged experts into slots (least recently used slot first), stream-ordered
-// before the next step, and updates the map.
+// over the host link inside the step.  After the step the host picks slots
+// for the flagged misses (least recently used first): the evicted experts'
+// map entries go back to their host copies before the next step starts, and
+// the copies into the slots run on a side stream (cudaMemcpyAsync) that
+// overlaps the next step; each entry switches to its slot (one 8-byte store
+// by a one-thread kernel) only after its copy has landed, so a concurrent
+// router reads either address, both valid.
 #pragma once
+#include <cuda_runtime.h>
+
 #include <cstdint>
 #include <vector>
 
@@ -28,6 +34,7 @@ struct Residency {
     unsigned char *used = nullptr;      // device [L][E]: experts read since the last update
     unsigned char *h_used = nullptr;    // pinned
     uint8_t *stage = nullptr;           // device: one expert, for loading
+    cudaStream_t side = nullptr;        // slot copies
     std::vector<std::vector<int>> owner;     // [L][slots] expert id or -1
     std::vector<std::vector<int>> slot_of;   // [L][E] slot or -1
     std::vector<std::vector<uint64_t>> last; // [L][E] update round of the last use
