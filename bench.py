@@ -22,6 +22,9 @@ full forward at positions 4096+.
   algorithmic bytes per launch = 4 experts x (gate_up tiles + gate_up bias).
 * cpu_baseline / --impl reference: the reference's own decode functions
   (oracle/_ref) on this host's cores, see oracle/cpu_baseline.py.
+* side measurements at N=1 (not the value): prefill (2048 ids in 1024-position
+  steps, expert and dense GEMMs on tcgen05), bs64 decode, and the
+  single-layer expert microbench of configs[1].
 
 Multi-GPU (torchrun): expert parallelism, experts split across ranks, the
 attention replicated; all ranks decode the same sequence (strong scaling).
@@ -214,6 +217,35 @@ def bs64_decode(m, ctx0, pos0, steps=16, warmup=3):
             "kernel_ms_per_step": {k: v[0] for k, v in prof.items()}}
 
 
+PREFILL_TOKENS = 2048
+PREFILL_CHUNK = 1024  # positions per prefill step: 4096 routed pairs, 32 per expert on average
+
+
+def prefill_bench(m, vocab, reps=2):
+    """Prompt encoding on the bs1 model (GPT-OSS-120B shape): PREFILL_TOKENS
+    seeded random ids through pc_prefill in steps of PREFILL_CHUNK positions.
+    The expert GEMMs run on tcgen05 (INT4 tiles dequantized to f16 in shared
+    memory, 32 routed rows per expert on average), the dense projections in
+    128-row tcgen05 blocks, attention over each row's causal positions.  Host
+    clock around pc_prefill (ids host->device, the next id back); per-kernel
+    device times from one profiled pass (CUDA events around each launch)."""
+    import numpy as np
+    import torch
+    ids = np.random.default_rng(7).integers(0, vocab, PREFILL_TOKENS).tolist()
+    m.prefill_tokens(ids, 0)  # warm-up
+    torch.cuda.synchronize()
+    t = time.perf_counter()
+    for _ in range(reps):
+        m.prefill_tokens(ids, 0)
+    dt = (time.perf_counter() - t) / reps
+    m.profile_begin()
+    m.prefill_tokens(ids, 0)
+    prof = m.profile_end()
+    return {"value": PREFILL_TOKENS / dt, "unit": "tok/s", "tokens": PREFILL_TOKENS, "chunk": PREFILL_CHUNK,
+            "ms": dt * 1e3, "timing": "host clock around pc_prefill (ids H2D, next id D2H)",
+            "kernel_ms": {k: v[0] for k, v in prof.items()}}
+
+
 def moe_micro(dev, iters=20):
     """one GPT-OSS-shaped expert layer (d_model 2880, FFN
     2880, 32 experts, INT4 gs32), M tokens routed to 4 experts each with
@@ -290,7 +322,8 @@ def main():
     t0 = time.time()
     extra = world == 1 and not args.no_extra
     m = Model.synthetic(cfg, seed=2024, ctx=ctx, device=local, ep_rank=rank, ep_size=world, nccl_id=nid,
-                        kv_bf16=KV_BF16, max_batch=BS64 if extra else 1)
+                        kv_bf16=KV_BF16, max_batch=BS64 if extra else 1,
+                        prefill_chunk=PREFILL_CHUNK if extra else 64)
     t_init = time.time() - t0
     m.kv_fill_synthetic(CTX_PREFIX)
     clk = Clocks(local)
@@ -373,6 +406,7 @@ def main():
         "clocks": clk.summary(),
     }
     if extra:
+        line["prefill"] = prefill_bench(m, cfg.vocab)
         line["bs64"] = bs64_decode(m, CTX_PREFIX, pos)
         m.close()
         line["moe_micro"] = moe_micro(local)

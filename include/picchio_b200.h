@@ -57,6 +57,9 @@ typedef struct {
     int use_graphs;    /* 1: replay decode steps as CUDA graphs */
     int expert_residency; /* 0: whole expert table in HBM; 1: pinned host + HBM cache */
     int expert_cache_slots; /* per layer, when expert_residency == 1 */
+    int prefill_chunk; /* positions per pc_prefill step without device sampling (default 64, the
+                          reference's PREFILL_BATCH); larger chunks put the expert GEMMs on the
+                          tensor cores (from 32 routed rows per expert); at most 4096 / topk */
 } pc_opts;
 
 /* Model shape (the fields cfg_load reads, picchio.c:349-425). */
@@ -85,7 +88,8 @@ typedef struct {
     int layer_type[256]; /* 0 sliding, 1 full (picchio.c:389-409) */
 } pc_model_cfg;
 
-/* Fills *o with the defaults (device 0, ctx 512, fp32 KV, batch 1, graphs on). */
+/* Fills *o with the defaults (device 0, ctx 512, fp32 KV, batch 1, graphs on,
+ * prefill chunks of 64). */
 void pc_default_opts(pc_opts *o);
 
 /* Status name and the calling thread's last error message. */

@@ -34,7 +34,7 @@ class PicchioError(RuntimeError):
 class _Opts(C.Structure):
     _fields_ = [("device", C.c_int), ("ctx_len", C.c_int), ("kv_bf16", C.c_int), ("max_batch", C.c_int),
                 ("ep_rank", C.c_int), ("ep_size", C.c_int), ("nccl_id", C.c_void_p), ("use_graphs", C.c_int),
-                ("expert_residency", C.c_int), ("expert_cache_slots", C.c_int)]
+                ("expert_residency", C.c_int), ("expert_cache_slots", C.c_int), ("prefill_chunk", C.c_int)]
 
 
 class _Cfg(C.Structure):
@@ -200,13 +200,14 @@ class Model:
     def __init__(self, model_dir: str | None = None, *, cfg: ModelConfig | None = None, seed: int = 0,
                  ctx: int = 512, kv_bf16: bool = False, max_batch: int = 1, device: int = 0,
                  use_graphs: bool = True, ep_rank: int = 0, ep_size: int = 1, nccl_id: bytes | None = None,
-                 expert_residency: int = 0, expert_cache_slots: int = 0):
+                 expert_residency: int = 0, expert_cache_slots: int = 0, prefill_chunk: int = 64):
         L = lib()
         o = _Opts()
         L.pc_default_opts(C.byref(o))
         o.device, o.ctx_len, o.kv_bf16, o.max_batch = device, ctx, int(kv_bf16), max_batch
         o.use_graphs, o.ep_rank, o.ep_size = int(use_graphs), ep_rank, ep_size
         o.expert_residency, o.expert_cache_slots = int(expert_residency), int(expert_cache_slots)
+        o.prefill_chunk = int(prefill_chunk)
         self._nid = C.create_string_buffer(nccl_id, 128) if nccl_id is not None else None
         o.nccl_id = C.cast(self._nid, C.c_void_p) if self._nid is not None else None
         h = C.c_void_p()

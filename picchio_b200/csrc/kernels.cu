@@ -603,7 +603,9 @@ cudaError_t launch_rmsnorm(const float *x, const float *w, float *out, int M, in
 cudaError_t launch_router(const RouterParams &r, cudaStream_t st) {
     // more pairs than one job table holds only with the expert-sorted pair
     // lists (the tensor-core expert path reads those, not the jobs)
-    if (r.E > 256 || r.K > 16 || r.M * r.K > (r.pair_start ? ROUTER_MAX_PAIRS : GEMV_MAX_JOBS))
+    // pairs are grouped at most 8 (or 4) per job: 4096 pairs of <= 256
+    // experts make at most 768 jobs, within GEMV_MAX_JOBS
+    if (r.E > 256 || r.K > 16 || r.M * r.K > ROUTER_MAX_PAIRS)
         return cudaErrorInvalidValue;
     if (r.ln_w && ((r.D & 3) || r.D > 4 * NORM_V4 * NORM_THREADS || !r.h_in || !r.hn_out)) return cudaErrorInvalidValue;
     const dim3 grid = r.sel_in ? dim3(1) : dim3((r.E + 1) / 2, (r.M + ROUTER_ROWS - 1) / ROUTER_ROWS);

@@ -4,6 +4,7 @@
 // per layer instead of a disk-fed LRU, RoPE tables, KV cache, step buffers.
 #include <cuda_bf16.h>
 
+#include <algorithm>
 #include <cmath>
 #include <cstdio>
 #include <cstring>
@@ -395,7 +396,10 @@ pc_status alloc_runtime(pc_ctx *c) {
     c->nseq = c->opts.max_batch > 0 ? c->opts.max_batch : 1;
     c->kv_ctx = c->opts.ctx_len > 0 ? c->opts.ctx_len : 512;
     if (c->kv_ctx > k.ctx_len) c->kv_ctx = k.ctx_len;  // picchio.c:2935
-    c->maxm = c->nseq > 64 ? c->nseq : 64;
+    c->maxm = std::max({c->nseq, 64, c->opts.prefill_chunk});
+    if ((int64_t)c->maxm * k.topk > ROUTER_MAX_PAIRS)
+        return fail(PC_ERR_RANGE, "max_batch / prefill_chunk above " + std::to_string(ROUTER_MAX_PAIRS / k.topk) +
+                                      " rows (" + std::to_string(ROUTER_MAX_PAIRS) + " routed pairs per step)");
     const int M = c->maxm;
     PC_TRY(rope_tables(c));
     const int kvd = KVH * hd;

@@ -220,13 +220,36 @@ void use_jobs(GemvParams &p, const DenseJobs *dj, int off, int cnt_idx) {
 // Launches with at most 8 input rows keep them all in the B operand.
 int shared_rows_for(int rows) { return rows <= GEMV_MAXR ? rows : 0; }
 
-bool use_tc(const pc_ctx *c, int M) { return c->tc.on && M >= TC_MIN_ROWS && M <= TC_MAX_ROWS; }
+bool use_tc(const pc_ctx *c, int M) { return c->tc.on && M >= TC_MIN_ROWS; }
+
+pc_status run_tc_block(pc_ctx *c, const GemvParams &g, const TcWeight *const *w, const float *const *bias, int nseg,
+                       int M, const char *label);
 
 // The dense projection described by g (epilogue fields set as for the GEMV)
-// over input rows 0..M-1 on the tensor cores: the rows' digit planes, then one
-// launch over the nseg weight matrices (q, k, v or a single one).
+// over input rows 0..M-1 on the tensor cores, TC_MAX_ROWS rows per launch (a
+// short last block included: the MMA tile is zero-padded, rows past it are
+// not stored).
 pc_status run_tc(pc_ctx *c, const GemvParams &g, const TcWeight *const *w, const float *const *bias, int nseg, int M,
                  const char *label) {
+    for (int r0 = 0; r0 < M; r0 += TC_MAX_ROWS) {
+        const int m = std::min(TC_MAX_ROWS, M - r0);
+        GemvParams b = g;
+        b.x = g.x + (size_t)r0 * g.ldx;
+        b.y = g.y ? g.y + (size_t)r0 * g.ldy : nullptr;
+        b.res_src = g.res_src ? g.res_src + (size_t)r0 * g.ldy : nullptr;
+        b.row_pos = g.row_pos ? g.row_pos + r0 : nullptr;
+        b.row_seq = g.row_seq ? g.row_seq + r0 : nullptr;
+        b.qbuf = g.qbuf ? g.qbuf + (size_t)r0 * g.ldq : nullptr;
+        b.argmax = g.argmax ? g.argmax + r0 : nullptr;
+        PC_TRY(run_tc_block(c, b, w, bias, nseg, m, label));
+    }
+    return PC_OK;
+}
+
+// One launch of at most TC_MAX_ROWS rows: the rows' digit planes, then the
+// tcgen05 GEMM over the nseg weight matrices (q, k, v or a single one).
+pc_status run_tc_block(pc_ctx *c, const GemvParams &g, const TcWeight *const *w, const float *const *bias, int nseg,
+                       int M, const char *label) {
     TcParams t;
     memset(&t, 0, sizeof t);
     int tiles = 0;
@@ -1057,6 +1080,7 @@ void pc_default_opts(pc_opts *o) {
     o->max_batch = 1;
     o->ep_size = 1;
     o->use_graphs = 1;
+    o->prefill_chunk = 64;
 }
 
 const char *pc_status_string(pc_status s) {
@@ -1162,7 +1186,9 @@ pc_status pc_prefill(pc_ctx *c, const int *ids, int n, int pos_base, int *next_t
     PC_TRY(check_ctx(c));
     if (!ids || !next_tok || n < 1) return fail(PC_ERR_INVALID_ARG, "empty prompt");
     if (pos_base < 0 || pos_base + n > c->kv_ctx) return fail(PC_ERR_RANGE, "prompt does not fit the KV capacity");
-    const int chunk = std::min(c->maxm, 64);
+    // with device sampling the blocks are the reference's 64 positions (each
+    // draws); otherwise opts.prefill_chunk positions per step
+    const int chunk = std::min(c->maxm, c->smp.on ? 64 : std::max(1, c->opts.prefill_chunk));
     std::vector<int> tok(chunk), ps(chunk);
     c->stages.clear();
     for (int off = 0; off < n; off += chunk) {

@@ -369,3 +369,28 @@ def test_expert_prefetch_makes_later_reads_hits(tmp_path):
     assert ids == m["ids_batched"][:16]
     assert st0["misses"] == 0 and st0["bytes_h2d"] > 0
     assert st1["misses"] == 0 and st1["hits"] > 0
+
+
+def test_large_prefill_chunks_on_tensor_cores_match_64_position_blocks(tmp_path):
+    """prefill_chunk = 300 (one step for a 300-position prompt): the dense
+    projections run as 128-row tcgen05 blocks (128 + 128 + 44 rows) and the
+    expert GEMMs on tcgen05 (75 routed rows per expert); the logits after the
+    prompt stay within the hidden-state bar of the 64-position blocks (GEMV
+    experts), and greedy decode continues identically."""
+    from picchio_b200 import Model
+    m = meta("tiny_gs32_i8")
+    d = str(tmp_path)
+    make_model(d, SynthConfig(**m["options"]), m["seed"])
+    ids = np.random.default_rng(3).integers(0, 1024, 300).tolist()
+    out = {}
+    for chunk in (64, 300):
+        with Model(d, ctx=m["ctx"], prefill_chunk=chunk) as model:
+            assert model.tensor_core_min_rows > 0
+            tok = model.prefill_tokens(ids, 0)
+            lg = model.logits(0)
+            toks = [tok]
+            for i in range(8):
+                toks.append(model.forward_token(toks[-1], 300 + i))
+            out[chunk] = (lg, toks)
+    assert rel_l2(out[300][0], out[64][0]) < HIDDEN_REL_L2
+    assert out[300][1] == out[64][1]
