@@ -133,6 +133,167 @@ __global__ void __launch_bounds__(NORM_THREADS) rmsnorm_kernel(const float *x, c
 // are added in a fixed order.  The last block to finish (atomic ticket) does
 // the top-k, the softmax and the expert job tables, reading the selection
 // from shared memory.
+// The expert job tables (and, with pair_start, the expert-sorted pair
+// lists) from the selection in ssel[0..P): pairs grouped by expert in
+// ascending pair order, at most per_job pairs per job.  Run by the 256
+// threads of the block that finishes the routing: a shared-memory histogram
+// of pairs per expert, scans, one warp placing the pairs 32 at a time (ranks
+// within a step from match-any groups), then one thread per expert filling
+// its jobs.  sorted: shared scratch of ROUTER_MAX_PAIRS ints.
+__device__ void router_jobs(const RouterParams &r, const int *ssel, int P, int *cnt, int *jstart, int *pstart,
+                            int *sorted) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
+    const int Ps = min(P, ROUTER_MAX_PAIRS);
+    const int pj = (r.per_job > 0 && r.per_job < GEMV_MAXR) ? r.per_job : GEMV_MAXR;
+    const int e = tid;
+    pstart[e] = 0;
+    __syncthreads();
+    for (int p = tid; p < Ps; p += blockDim.x) {
+        const int ep = ssel[p];
+        const bool loc = ep >= r.e_lo && ep < r.e_hi;
+        r.pair_local[p] = loc ? 1 : 0;
+        if (loc) atomicAdd(&pstart[ep], 1);
+    }
+    __syncthreads();
+    const int n = e < r.E ? pstart[e] : 0;  // pairs of local expert e
+    cnt[e] = (n + pj - 1) / pj;
+    __syncthreads();
+    if (warp == 1) {  // exclusive scan of pairs per expert: 8 experts per lane
+        int v[8], tot = 0;
+#pragma unroll
+        for (int q = 0; q < 8; ++q) { v[q] = tot; tot += pstart[lane * 8 + q]; }
+        int inc = tot;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int nn = __shfl_up_sync(0xffffffffu, inc, o);
+            if (lane >= o) inc += nn;
+        }
+        const int base = inc - tot;
+        __syncwarp();
+#pragma unroll
+        for (int q = 0; q < 8; ++q) pstart[lane * 8 + q] = base + v[q];
+        if (lane == 31) pstart[256] = inc;
+    }
+    if (warp == 0) {  // exclusive scan of jobs per expert
+        int v[8], tot = 0;
+#pragma unroll
+        for (int q = 0; q < 8; ++q) { v[q] = tot; tot += cnt[lane * 8 + q]; }
+        int inc = tot;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int nn = __shfl_up_sync(0xffffffffu, inc, o);
+            if (lane >= o) inc += nn;
+        }
+        const int base = inc - tot;
+#pragma unroll
+        for (int q = 0; q < 8; ++q) jstart[lane * 8 + q] = base + v[q];
+        if (lane == 31) {
+            jstart[256] = inc;
+            r.njobs[0] = r.njobs[1] = min(inc, GEMV_MAX_JOBS);
+        }
+    }
+    __syncthreads();
+    if (warp == 0) {  // stable placement; cnt becomes the running offset per expert
+#pragma unroll
+        for (int q = 0; q < 8; ++q) cnt[lane * 8 + q] = 0;
+        __syncwarp();
+        for (int b = 0; b < Ps; b += 32) {
+            const int p = b + lane;
+            const int ep = p < Ps ? ssel[p] : -1;
+            const bool loc = ep >= r.e_lo && ep < r.e_hi;
+            const unsigned grp = __match_any_sync(0xffffffffu, loc ? ep : -1);
+            int off = 0;
+            if (loc) {
+                off = cnt[ep];
+                sorted[pstart[ep] + off + __popc(grp & ((1u << lane) - 1u))] = p;
+            }
+            __syncwarp();
+            if (loc && lane == 31 - __clz(grp)) cnt[ep] = off + __popc(grp);
+            __syncwarp();
+        }
+    }
+    __syncthreads();
+    if (r.pair_start) {
+        if (e < r.E) r.pair_start[e] = pstart[e];
+        if (e == 0) r.pair_start[r.E] = pstart[256];
+        for (int q = tid; q < pstart[256]; q += blockDim.x) r.pair_list[q] = sorted[q];
+    }
+    if (n == 0) return;
+    if (r.used) r.used[e] = 1;
+    const uint8_t *base = r.emap ? r.emap[e] : r.table + (int64_t)(e - r.e_lo) * r.stride;
+    const int *mine = sorted + pstart[e];
+    for (int k = 0; k * pj < n; ++k) {
+        const int j = jstart[e] + k;
+        if (j >= GEMV_MAX_JOBS) break;
+        const int fill = min(pj, n - k * pj);
+        GemvJob &gu = r.jobs_gu[j];
+        GemvJob &dn = r.jobs_dn[j];
+        gu.tiles = base + r.off_gu;
+        gu.rs = r.off_gu_rs >= 0 ? reinterpret_cast<const float *>(base + r.off_gu_rs) : nullptr;
+        gu.bias = r.off_gu_b >= 0 ? reinterpret_cast<const float *>(base + r.off_gu_b) : nullptr;
+        gu.n_rt = r.gu_rt; gu.O = r.gu_O; gu.seg = 0;
+        dn.tiles = base + r.off_dn;
+        dn.rs = r.off_dn_rs >= 0 ? reinterpret_cast<const float *>(base + r.off_dn_rs) : nullptr;
+        dn.bias = r.off_dn_b >= 0 ? reinterpret_cast<const float *>(base + r.off_dn_b) : nullptr;
+        dn.n_rt = r.dn_rt; dn.O = r.dn_O; dn.seg = 0;
+        for (int f = 0; f < fill; ++f) {
+            const int p = mine[k * pj + f];
+            gu.in_row[f] = p / r.K;
+            gu.out_row[f] = p;
+            dn.in_row[f] = p;
+            dn.out_row[f] = p;
+        }
+        gu.nrows = dn.nrows = fill;
+    }
+}
+
+// Top-k of row m from its E logits lg (global memory: read past L1; else
+// shared memory), one warp: K rounds of strict '>' argmax, ties to the lowest
+// index (picchio.c:1330-1340), then the softmax over the K selected logits
+// (quant.h:406-412).  Writes sel and w (and ssel when not null).
+template <bool GLOBAL>
+__device__ void router_topk_row(const RouterParams &r, const float *lg, int m, int *ssel) {
+    const int lane = threadIdx.x & 31;
+    float vals[8];
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+        const int e = lane + 32 * q;
+        vals[q] = e < r.E ? (GLOBAL ? __ldcg(lg + e) : lg[e]) : -INFINITY;
+    }
+    float wk[16];
+    int sk[16];
+    for (int k = 0; k < r.K; ++k) {
+        float bv = -1e30f;
+        int bi = -1;
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+            const int e = lane + 32 * q;
+            if (e < r.E && vals[q] > bv) { bv = vals[q]; bi = e; }
+        }
+        for (int o = 16; o > 0; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+            if (ov > bv || (ov == bv && oi >= 0 && (bi < 0 || oi < bi))) { bv = ov; bi = oi; }
+        }
+        sk[k < 16 ? k : 15] = bi;
+        wk[k < 16 ? k : 15] = bv;
+#pragma unroll
+        for (int q = 0; q < 8; ++q)
+            if (bi >= 0 && bi == lane + 32 * q) vals[q] = -INFINITY;
+    }
+    if (lane == 0) {
+        float mx = -1e30f;
+        for (int k = 0; k < r.K; ++k) if (wk[k] > mx) mx = wk[k];
+        float sum = 0.0f;
+        for (int k = 0; k < r.K; ++k) { wk[k] = expf(__fsub_rn(wk[k], mx)); sum = __fadd_rn(sum, wk[k]); }
+        for (int k = 0; k < r.K; ++k) {
+            r.sel[m * r.K + k] = sk[k];
+            if (ssel && m * r.K + k < ROUTER_MAX_PAIRS) ssel[m * r.K + k] = sk[k];
+            r.w[m * r.K + k] = __fdiv_rn(wk[k], sum);
+        }
+    }
+}
+
 constexpr int ROUTER_RV = 6;    // float4 per lane per operand in flight
 constexpr int ROUTER_ROWS = 2;  // input rows per block (blockIdx.y = row group)
 
@@ -142,7 +303,7 @@ __global__ void __launch_bounds__(256) router_kernel(const RouterParams r) {
     __shared__ bool last;
     __shared__ float part[8];
     __shared__ int cnt[256], jstart[257], pstart[257];
-    __shared__ int ssel[ROUTER_MAX_PAIRS];
+    __shared__ int ssel[ROUTER_MAX_PAIRS], sorted[ROUTER_MAX_PAIRS];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int P = r.M * r.K;
     if (!r.sel_in) {
@@ -247,48 +408,7 @@ __global__ void __launch_bounds__(256) router_kernel(const RouterParams r) {
         if (!last) return;
         __threadfence();
         // top-k, K rounds of strict '>' argmax; ties -> lowest index
-        for (int m = warp; m < r.M; m += 8) {
-            const float *lg = r.logits + (int64_t)m * r.E;
-            float vals[8];
-#pragma unroll
-            for (int q = 0; q < 8; ++q) {
-                const int e = lane + 32 * q;
-                vals[q] = e < r.E ? __ldcg(lg + e) : -INFINITY;
-            }
-            float wk[16];
-            int sk[16];
-            for (int k = 0; k < r.K; ++k) {
-                float bv = -1e30f;
-                int bi = -1;
-#pragma unroll
-                for (int q = 0; q < 8; ++q) {
-                    const int e = lane + 32 * q;
-                    if (e < r.E && vals[q] > bv) { bv = vals[q]; bi = e; }
-                }
-                for (int o = 16; o > 0; o >>= 1) {
-                    const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-                    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-                    if (ov > bv || (ov == bv && oi >= 0 && (bi < 0 || oi < bi))) { bv = ov; bi = oi; }
-                }
-                sk[k < 16 ? k : 15] = bi;
-                wk[k < 16 ? k : 15] = bv;
-#pragma unroll
-                for (int q = 0; q < 8; ++q)
-                    if (bi >= 0 && bi == lane + 32 * q) vals[q] = -INFINITY;
-            }
-            if (lane == 0) {
-                // softmax over the K selected logits (quant.h:406-412)
-                float mx = -1e30f;
-                for (int k = 0; k < r.K; ++k) if (wk[k] > mx) mx = wk[k];
-                float sum = 0.0f;
-                for (int k = 0; k < r.K; ++k) { wk[k] = expf(__fsub_rn(wk[k], mx)); sum = __fadd_rn(sum, wk[k]); }
-                for (int k = 0; k < r.K; ++k) {
-                    r.sel[m * r.K + k] = sk[k];
-                    if (m * r.K + k < ROUTER_MAX_PAIRS) ssel[m * r.K + k] = sk[k];
-                    r.w[m * r.K + k] = __fdiv_rn(wk[k], sum);
-                }
-            }
-        }
+        for (int m = warp; m < r.M; m += 8) router_topk_row<true>(r, r.logits + (int64_t)m * r.E, m, ssel);
         __syncthreads();
     } else {
         if (blockIdx.x != 0) return;
@@ -300,91 +420,152 @@ __global__ void __launch_bounds__(256) router_kernel(const RouterParams r) {
         }
         __syncthreads();
     }
-    // expert job tables: pairs grouped by expert, at most pj pairs per job
-    const int Ps = min(P, ROUTER_MAX_PAIRS);
-    const int pj = (r.per_job > 0 && r.per_job < GEMV_MAXR) ? r.per_job : GEMV_MAXR;
-    const int e = threadIdx.x;
-    int n = 0;
-    if (e < r.E && e >= r.e_lo && e < r.e_hi) {
-        for (int p = 0; p < Ps; ++p) n += (ssel[p] == e);
+    router_jobs(r, ssel, P, cnt, jstart, pstart, sorted);
+}
+
+// Many rows (batched decode, prefill): one block per RB rows instead.  The
+// block normalises its rows once into shared memory (rmsnorm_kernel's
+// arithmetic), then warp w takes experts w, w + 8, ... and forms each
+// (row, expert) dot exactly as router_kernel does (four quarters of D, lanes
+// strided by 32 float4 with four component sums, the same shuffle tree, the
+// quarters added as (q0 + q1) + (q2 + q3)), so the logits are bit-identical;
+// the next quarter's R loads are in flight while a quarter is summed.  Each
+// block takes the top-k of its own rows; the last block (ticket) builds the
+// job tables.  D % 4 == 0 and one 32 x ROUTER_RV float4 pass per quarter
+// (D <= 3072).
+constexpr int ROUTER_RB_MIN_ROWS = 256;  // from this many rows the row-block form is used
+
+// Row-block router helpers: R of task t ((expert warp + 8 (t / 4), quarter
+// t % 4)) into registers, and the task's dots for the block's RB rows.
+__device__ __forceinline__ void rr_load(const RouterParams &r, int n4, int warp, int lane, int t,
+                                        float4 (&rv)[ROUTER_RV]) {
+    const int e = warp + 8 * (t >> 2), q = t & 3;
+    const int i0 = n4 * q / 4, i1 = n4 * (q + 1) / 4;
+    const float4 *r4 = reinterpret_cast<const float4 *>(r.R + (int64_t)e * r.D);
+#pragma unroll
+    for (int j = 0; j < ROUTER_RV; ++j) {
+        const int i = i0 + lane + 32 * j;
+        rv[j] = i < i1 ? r4[i] : make_float4(0.f, 0.f, 0.f, 0.f);
     }
-    cnt[e] = (n + pj - 1) / pj;
-    pstart[e] = n;
+}
+
+template <int RB>
+__device__ __forceinline__ void rr_task(const RouterParams &r, const float4 *xn4, int n4, int warp, int lane, int t,
+                                        int nr, int m0, const float4 (&rv)[ROUTER_RV], float (&p0)[RB],
+                                        float (&a01)[RB], float (&p2)[RB], float *lgs) {
+    const int e = warp + 8 * (t >> 2), q = t & 3;
+    const int i0 = n4 * q / 4, i1 = n4 * (q + 1) / 4;
+#pragma unroll
+    for (int rr = 0; rr < RB; ++rr) {
+        float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+        const float4 *xr = xn4 + (size_t)rr * n4;
+#pragma unroll
+        for (int j = 0; j < ROUTER_RV; ++j) {
+            const int i = i0 + lane + 32 * j;
+            const float4 xv = i < i1 ? xr[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+            s0 = __fmaf_rn(xv.x, rv[j].x, s0);
+            s1 = __fmaf_rn(xv.y, rv[j].y, s1);
+            s2 = __fmaf_rn(xv.z, rv[j].z, s2);
+            s3 = __fmaf_rn(xv.w, rv[j].w, s3);
+        }
+        float v = __fadd_rn(__fadd_rn(s0, s1), __fadd_rn(s2, s3));
+        for (int o = 16; o > 0; o >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, o));
+        v = __shfl_sync(0xffffffffu, v, 0);  // lane 0's sum, the one router_kernel keeps
+        if (q == 0) {
+            p0[rr] = v;
+        } else if (q == 1) {
+            a01[rr] = __fadd_rn(p0[rr], v);
+        } else if (q == 2) {
+            p2[rr] = v;
+        } else if (lane == 0 && rr < nr) {
+            float lv = __fadd_rn(a01[rr], __fadd_rn(p2[rr], v));
+            if (r.bias) lv = r.bias_first ? __fadd_rn(r.bias[e], lv) : __fadd_rn(lv, r.bias[e]);
+            lgs[rr * 256 + e] = lv;
+            r.logits[(int64_t)(m0 + rr) * r.E + e] = lv;
+        }
+    }
+}
+
+template <int RB>
+__global__ void __launch_bounds__(256) router_rows_kernel(const RouterParams r) {
+    extern __shared__ float4 rsm4[];
+    float4 *xn4 = rsm4;  // [RB][D / 4]
+    __shared__ float lgs[RB][256];
+    __shared__ bool last;
+    __shared__ int cnt[256], jstart[257], pstart[257];
+    __shared__ int ssel[ROUTER_MAX_PAIRS], sorted[ROUTER_MAX_PAIRS];
+    pdl_wait();
+    pdl_trigger();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
+    const int m0 = blockIdx.x * RB, nr = min(RB, r.M - m0);
+    const int n4 = r.D >> 2;
+    const float4 z4 = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int rr = 0; rr < RB; ++rr) {
+        float4 *dst = xn4 + (size_t)rr * n4;
+        if (rr >= nr) {
+            for (int i = tid; i < n4; i += NORM_THREADS) dst[i] = z4;
+            continue;
+        }
+        const int m = m0 + rr;
+        if (r.ln_w) {
+            const float4 *h4 = reinterpret_cast<const float4 *>(r.h_in + (int64_t)m * r.D);
+            const float4 *w4 = reinterpret_cast<const float4 *>(r.ln_w);
+            float4 hv[NORM_V4];
+            double ss = 0.0;
+#pragma unroll
+            for (int j = 0; j < NORM_V4; ++j) {
+                const int i = tid + j * NORM_THREADS;
+                hv[j] = i < n4 ? h4[i] : z4;
+                ss += (double)hv[j].x * hv[j].x + (double)hv[j].y * hv[j].y + (double)hv[j].z * hv[j].z +
+                      (double)hv[j].w * hv[j].w;
+            }
+            const float rn = norm_scale(ss, r.D, r.eps);
+            float4 *o4 = reinterpret_cast<float4 *>(r.hn_out + (int64_t)m * r.D);
+#pragma unroll
+            for (int j = 0; j < NORM_V4; ++j) {
+                const int i = tid + j * NORM_THREADS;
+                if (i < n4) {
+                    const float4 w = w4[i];
+                    const float4 v = make_float4(__fmul_rn(__fmul_rn(hv[j].x, rn), w.x), __fmul_rn(__fmul_rn(hv[j].y, rn), w.y),
+                                                 __fmul_rn(__fmul_rn(hv[j].z, rn), w.z), __fmul_rn(__fmul_rn(hv[j].w, rn), w.w));
+                    dst[i] = v;
+                    o4[i] = v;
+                }
+            }
+        } else {
+            const float4 *x4 = reinterpret_cast<const float4 *>(r.x + (int64_t)m * r.D);
+            for (int i = tid; i < n4; i += NORM_THREADS) dst[i] = x4[i];
+        }
+    }
     __syncthreads();
-    if (r.pair_start && warp == 1) {  // exclusive scan of pairs per expert
-        int v[8], tot = 0;
-#pragma unroll
-        for (int q = 0; q < 8; ++q) { v[q] = tot; tot += pstart[lane * 8 + q]; }
-        int inc = tot;
-#pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-            const int nn = __shfl_up_sync(0xffffffffu, inc, o);
-            if (lane >= o) inc += nn;
-        }
-        const int base = inc - tot;
-        __syncwarp();
-#pragma unroll
-        for (int q = 0; q < 8; ++q) pstart[lane * 8 + q] = base + v[q];
-        if (lane == 31) pstart[256] = inc;
-    }
-    if (warp == 0) {  // exclusive scan of jobs per expert: 8 experts per lane
-        int v[8], tot = 0;
-#pragma unroll
-        for (int q = 0; q < 8; ++q) { v[q] = tot; tot += cnt[lane * 8 + q]; }
-        int inc = tot;
-#pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-            const int nn = __shfl_up_sync(0xffffffffu, inc, o);
-            if (lane >= o) inc += nn;
-        }
-        const int base = inc - tot;
-#pragma unroll
-        for (int q = 0; q < 8; ++q) jstart[lane * 8 + q] = base + v[q];
-        if (lane == 31) {
-            jstart[256] = inc;
-            r.njobs[0] = r.njobs[1] = min(inc, GEMV_MAX_JOBS);
+    // (expert, quarter) tasks of this warp, R of the next task in flight
+    const int ne = (r.E - warp + 7) / 8, T = 4 * max(ne, 0);
+    float4 ra[ROUTER_RV], rb[ROUTER_RV];
+    float p0[RB], a01[RB], p2[RB];
+    if (T > 0) rr_load(r, n4, warp, lane, 0, ra);
+    for (int t = 0; t < T; t += 2) {
+        if (t + 1 < T) rr_load(r, n4, warp, lane, t + 1, rb);
+        rr_task<RB>(r, xn4, n4, warp, lane, t, nr, m0, ra, p0, a01, p2, &lgs[0][0]);
+        if (t + 1 < T) {
+            if (t + 2 < T) rr_load(r, n4, warp, lane, t + 2, ra);
+            rr_task<RB>(r, xn4, n4, warp, lane, t + 1, nr, m0, rb, p0, a01, p2, &lgs[0][0]);
         }
     }
     __syncthreads();
-    for (int p = threadIdx.x; p < Ps; p += blockDim.x) {
-        const int ep = ssel[p];
-        r.pair_local[p] = (ep >= r.e_lo && ep < r.e_hi) ? 1 : 0;
+    for (int rr = warp; rr < nr; rr += 8) router_topk_row<false>(r, lgs[rr], m0 + rr, nullptr);
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) {
+        last = atomicAdd(r.counter, 1u) == gridDim.x - 1;
+        if (last) *r.counter = 0u;
     }
-    if (r.pair_start) {
-        if (e < r.E) r.pair_start[e] = pstart[e];
-        if (e == 0) r.pair_start[r.E] = pstart[256];
-        if (n > 0) {
-            int q = pstart[e];
-            for (int p = 0; p < Ps; ++p)
-                if (ssel[p] == e) r.pair_list[q++] = p;
-        }
-    }
-    if (n == 0) return;
-    if (r.used) r.used[e] = 1;
-    const uint8_t *base = r.emap ? r.emap[e] : r.table + (int64_t)(e - r.e_lo) * r.stride;
-    int j = jstart[e], fill = 0;
-    for (int p = 0; p < Ps && j < GEMV_MAX_JOBS; ++p) {
-        if (ssel[p] != e) continue;
-        GemvJob &gu = r.jobs_gu[j];
-        GemvJob &dn = r.jobs_dn[j];
-        if (fill == 0) {
-            gu.tiles = base + r.off_gu;
-            gu.rs = r.off_gu_rs >= 0 ? reinterpret_cast<const float *>(base + r.off_gu_rs) : nullptr;
-            gu.bias = r.off_gu_b >= 0 ? reinterpret_cast<const float *>(base + r.off_gu_b) : nullptr;
-            gu.n_rt = r.gu_rt; gu.O = r.gu_O; gu.seg = 0;
-            dn.tiles = base + r.off_dn;
-            dn.rs = r.off_dn_rs >= 0 ? reinterpret_cast<const float *>(base + r.off_dn_rs) : nullptr;
-            dn.bias = r.off_dn_b >= 0 ? reinterpret_cast<const float *>(base + r.off_dn_b) : nullptr;
-            dn.n_rt = r.dn_rt; dn.O = r.dn_O; dn.seg = 0;
-        }
-        gu.in_row[fill] = p / r.K;
-        gu.out_row[fill] = p;
-        dn.in_row[fill] = p;
-        dn.out_row[fill] = p;
-        ++fill;
-        gu.nrows = dn.nrows = fill;
-        if (fill == pj) { fill = 0; ++j; }
-    }
+    __syncthreads();
+    if (!last) return;
+    __threadfence();
+    const int P = r.M * r.K, Ps = min(P, ROUTER_MAX_PAIRS);
+    for (int p = tid; p < Ps; p += blockDim.x) ssel[p] = __ldcg(r.sel + p);
+    __syncthreads();
+    router_jobs(r, ssel, P, cnt, jstart, pstart, sorted);
 }
 
 // -------------------------------------------------------------- combine ----
@@ -608,9 +789,25 @@ cudaError_t launch_router(const RouterParams &r, cudaStream_t st) {
     if (r.E > 256 || r.K > 16 || r.M * r.K > ROUTER_MAX_PAIRS)
         return cudaErrorInvalidValue;
     if (r.ln_w && ((r.D & 3) || r.D > 4 * NORM_V4 * NORM_THREADS || !r.h_in || !r.hn_out)) return cudaErrorInvalidValue;
+    if (!r.sel_in && r.M >= ROUTER_RB_MIN_ROWS && (r.D & 3) == 0 && r.D <= 4 * 32 * ROUTER_RV * 4 &&
+        r.D <= 4 * NORM_V4 * NORM_THREADS) {
+        const int rb = r.M >= 256 ? 4 : 2;  // at least ~64 blocks
+        const dim3 grid((r.M + rb - 1) / rb);
+        const size_t smem = (size_t)rb * r.D * 4;
+        return rb == 4 ? launch_k(router_rows_kernel<4>, grid, dim3(256), smem, st, r)
+                       : launch_k(router_rows_kernel<2>, grid, dim3(256), smem, st, r);
+    }
     const dim3 grid = r.sel_in ? dim3(1) : dim3((r.E + 1) / 2, (r.M + ROUTER_ROWS - 1) / ROUTER_ROWS);
     return launch_k(router_kernel, grid, dim3(256), 0, st, r);
     return cudaGetLastError();
+}
+
+cudaError_t kernels_configure() {
+    // the row-block router keeps RB normalised rows of up to 3072 floats
+    cudaError_t e = cudaFuncSetAttribute(router_rows_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, 2 * 3072 * 4);
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(router_rows_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, 4 * 3072 * 4);
+    return e;
 }
 
 cudaError_t launch_combine(const float *eo, const float *w, const int *sel, float scale, int M, int K,

@@ -81,6 +81,8 @@ struct RouterParams {
 // (picchio.c:1330-1340), softmax over the k logits (picchio.c:1355), and the
 // per-expert job tables of the two expert GEMVs.
 cudaError_t launch_router(const RouterParams &r, cudaStream_t st);
+// Kernel attributes (shared-memory limits) once per device.
+cudaError_t kernels_configure();
 
 // out[m][i] = sum over k (in k order) of w[m][k]*scale * eo[m*K+k][i]
 // (picchio.c:1445-1454); h[m][i] += out[m][i] when h != null.  With ln_w

@@ -55,6 +55,7 @@ pc_status device_setup(int dev, int *nsm, int *max_smem) {
         PC_CU(gemv_configure(*max_smem));
         PC_CU(decode_configure(*max_smem));
         PC_CU(tc_configure());
+        PC_CU(kernels_configure());
         g_configured[dev] = true;
     }
     return PC_OK;

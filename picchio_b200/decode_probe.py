@@ -1,10 +1,13 @@
 """A few decode steps of a GPT-OSS-120B-shaped model with fewer layers,
 without CUDA graphs: the small, repeatable workload the ncu captures under
 ``profiles/`` run (each kernel launch is then visible on its own).  With
---batch B > 1 every step is one pc_decode_batch over B sequences.
+--batch B > 1 every step is one pc_decode_batch over B sequences; with
+--prefill N the probe instead encodes N seeded random ids in steps of
+--chunk positions (pc_prefill).
 
     python -m picchio_b200.decode_probe --layers 2 --steps 4
     python -m picchio_b200.decode_probe --layers 2 --steps 2 --batch 64
+    python -m picchio_b200.decode_probe --layers 1 --prefill 1024 --chunk 1024
 """
 from __future__ import annotations
 
@@ -17,7 +20,19 @@ def main() -> None:
     ap.add_argument("--steps", type=int, default=4)
     ap.add_argument("--context", type=int, default=4096)
     ap.add_argument("--batch", type=int, default=1)
+    ap.add_argument("--prefill", type=int, default=0)
+    ap.add_argument("--chunk", type=int, default=64)
     args = ap.parse_args()
+    if args.prefill > 0:
+        import numpy as np
+        from picchio_b200 import Model, ModelConfig
+        cfg = ModelConfig.gpt_oss_120b()
+        cfg.n_layers = args.layers
+        m = Model.synthetic(cfg, seed=1, ctx=args.prefill + 8, use_graphs=False, kv_bf16=True,
+                            prefill_chunk=args.chunk)
+        ids = np.random.default_rng(7).integers(0, cfg.vocab, args.prefill).tolist()
+        print("ok", m.prefill_tokens(ids, 0))
+        return
     from picchio_b200 import Model, ModelConfig
     cfg = ModelConfig.gpt_oss_120b()
     cfg.n_layers = args.layers

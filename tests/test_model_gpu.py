@@ -394,3 +394,22 @@ def test_large_prefill_chunks_on_tensor_cores_match_64_position_blocks(tmp_path)
             out[chunk] = (lg, toks)
     assert rel_l2(out[300][0], out[64][0]) < HIDDEN_REL_L2
     assert out[300][1] == out[64][1]
+
+
+def test_row_block_router_matches_single_row_router(variant):
+    """From 16 rows the router takes whole rows per block (row-block kernel);
+    one row uses the expert-parallel kernel.  Both form each dot in the same
+    order, so 48 rows routed together give the outputs of the same rows
+    routed one at a time."""
+    import torch
+    from picchio_b200 import Model
+    m, d = variant
+    rng = np.random.default_rng(11)
+    with Model(d, ctx=64, max_batch=64) as model:
+        D = model.config["hidden"]
+        x = rng.standard_normal((48, D)).astype(np.float32)
+        for layer in range(model.config["n_layers"]):
+            batch = model.moe_forward(torch.from_numpy(x).cuda(), layer).cpu().numpy()
+            for r in range(48):
+                one = model.moe_forward(torch.from_numpy(x[r:r + 1]).cuda(), layer).cpu().numpy()[0]
+                assert rel_l2(batch[r], one) < 1e-6, (layer, r)
