@@ -28,6 +28,7 @@ cudaError_t launch_hd(const AttnParams &a, dim3 grid, cudaStream_t st) {
 
 cudaError_t launch_attention(const AttnParams &a, cudaStream_t st) {
     if (a.H / a.KVH > MAXG || a.nsplit > 64) return cudaErrorInvalidValue;
+    if (attention_tc_ok(a)) return launch_attention_tc(a, st);
     dim3 grid(a.nsplit, a.KVH, a.M);
     return a.kv_bf16 ? launch_hd<__nv_bfloat16>(a, grid, st) : launch_hd<float>(a, grid, st);
 }

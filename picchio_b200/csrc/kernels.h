@@ -37,6 +37,13 @@ struct AttnParams {
 constexpr int ATTN_SPLIT = 256;
 // gqa_attention's score / softmax-with-sink / P.V part (picchio.c:556-607).
 cudaError_t launch_attention(const AttnParams &a, cudaStream_t st);
+// The tensor-core form (attention_tc.cu) for steps of ATTN_TC_MIN_ROWS rows
+// or more with a bf16 KV cache, head size 64 and 8 query heads per KV head;
+// launch_attention picks it when attention_tc_ok.
+constexpr int ATTN_TC_MIN_ROWS = 16;
+bool attention_tc_ok(const AttnParams &a);
+cudaError_t attention_tc_configure();
+cudaError_t launch_attention_tc(const AttnParams &a, cudaStream_t st);
 
 constexpr int ROUTER_MAX_PAIRS = 4096;  // (row, k) pairs one router launch sorts by expert
 

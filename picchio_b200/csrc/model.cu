@@ -56,6 +56,7 @@ pc_status device_setup(int dev, int *nsm, int *max_smem) {
         PC_CU(decode_configure(*max_smem));
         PC_CU(tc_configure());
         PC_CU(kernels_configure());
+        PC_CU(attention_tc_configure());
         g_configured[dev] = true;
     }
     return PC_OK;

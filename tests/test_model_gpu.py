@@ -413,3 +413,56 @@ def test_row_block_router_matches_single_row_router(variant):
             for r in range(48):
                 one = model.moe_forward(torch.from_numpy(x[r:r + 1]).cuda(), layer).cpu().numpy()[0]
                 assert rel_l2(batch[r], one) < 1e-6, (layer, r)
+
+
+_GPTOSS_HEADS_DIR = []
+
+
+def _gptoss_heads_model(**kw):
+    """A small seeded model with GPT-OSS attention heads (head size 64, 8
+    query heads per KV head), the shape the tensor-core attention serves,
+    with a bf16 KV cache."""
+    import tempfile
+    from picchio_b200 import Model
+    if not _GPTOSS_HEADS_DIR:
+        d = tempfile.mkdtemp()
+        make_model(d, SynthConfig(num_attention_heads=16, num_key_value_heads=2, head_dim=64), 1234)
+        _GPTOSS_HEADS_DIR.append(d)
+    return Model(_GPTOSS_HEADS_DIR[0], kv_bf16=True, **kw)
+
+
+def test_tensor_core_attention_batch_matches_single_rows():
+    """32 sequences at 600 cached positions (window layer and full layer):
+    the batch step runs the tensor-core attention (Q and P as bf16 hi + lo
+    halves against the bf16 cache); rows 0, 7 and 31 equal the same
+    sequences decoded alone (the fp32 one-row kernel): same next id, logits
+    within 1e-3."""
+    B, n = 32, 600
+    toks = [(7 * s + 3) % 1000 for s in range(B)]
+    with _gptoss_heads_model(ctx=n + 8, max_batch=B) as b:
+        for s in range(B):
+            b.kv_fill_synthetic(n, seq=s, seed=200 + s)
+        nxt = b.decode_batch(toks, [n] * B)
+        lb = {s: b.logits(s) for s in (0, 7, 31)}
+    with _gptoss_heads_model(ctx=n + 8) as a:
+        for s in (0, 7, 31):
+            a.kv_fill_synthetic(n, seq=0, seed=200 + s)
+            t = a.forward_token(toks[s], n)
+            assert t == nxt[s], s
+            assert rel_l2(lb[s], a.logits(0)) < 1e-3, s
+
+
+def test_tensor_core_attention_prefill_matches_sequential_forward():
+    """A 200-position prompt in 64-position prefill steps (tensor-core
+    attention over each row's causal positions) against 200 one-token steps:
+    the same next id, logits within 1e-3."""
+    ids = np.random.default_rng(5).integers(0, 1024, 200).tolist()
+    with _gptoss_heads_model(ctx=256) as a:
+        t_pre = a.prefill_tokens(ids, 0)
+        l_pre = a.logits(0)
+    with _gptoss_heads_model(ctx=256) as b:
+        for i, tok in enumerate(ids):
+            t_seq = b.forward_token(tok, i)
+        l_seq = b.logits(0)
+    assert t_pre == t_seq
+    assert rel_l2(l_pre, l_seq) < 1e-3
