@@ -609,10 +609,17 @@ pc_status synth_model(pc_ctx *c, uint64_t seed) {
     const int D = k.hidden, H = k.n_heads, KVH = k.n_kv_heads, hd = k.head_dim, E = k.n_experts;
     const int I2 = 2 * k.intermediate, V = k.vocab;
     cudaStream_t st = c->st;
-    int64_t tmpb = std::max<int64_t>((int64_t)V * D, (int64_t)I2 * D) + (int64_t)V * 4 + (int64_t)I2 * (D / 8 + 2) * 4 + 4096;
+    // scratch for the row-major matrix being generated and its scales: the
+    // largest of every matrix generated below (embedding / lm_head, q and o
+    // projections, expert gate_up and down), scales for gs >= 8
+    const int64_t big = std::max({(int64_t)V * D, (int64_t)I2 * D, (int64_t)H * hd * D,
+                                  (int64_t)D * k.intermediate});
+    const int64_t max_rows = std::max({(int64_t)V, (int64_t)I2, (int64_t)H * hd, (int64_t)D});
+    const int64_t max_cols = std::max({(int64_t)D, (int64_t)H * hd, (int64_t)k.intermediate});
+    const int64_t soff = align256(big);
+    int64_t tmpb = soff + max_rows * (max_cols / 8 + 2) * 4 + 4096;
     uint8_t *tmp = nullptr;
     PC_CU(cudaMalloc(&tmp, tmpb));
-    const int64_t soff = align256(std::max<int64_t>((int64_t)V * D, (int64_t)I2 * D));
     float *tmps = reinterpret_cast<float *>(tmp + soff);
     uint64_t tag = 0;
     auto dense = [&](int O, int I, int perm, int hdim, TileDesc &t, int fmt, int gs) -> pc_status {

@@ -466,3 +466,18 @@ def test_tensor_core_attention_prefill_matches_sequential_forward():
         l_seq = b.logits(0)
     assert t_pre == t_seq
     assert rel_l2(l_pre, l_seq) < 1e-3
+
+
+def test_synthetic_model_with_wide_attention_is_finite():
+    """pc_init_synthetic for a shape whose q projection (64 heads x 64 x 512)
+    is larger than its embedding (1024 x 512): the generation scratch covers
+    every matrix, so the weights (and the logits of a few steps) are finite."""
+    from picchio_b200 import Model, ModelConfig
+    cfg = ModelConfig(hidden=512, n_layers=2, n_heads=64, n_kv_heads=8, head_dim=64, n_experts=8, topk=2,
+                      intermediate=256, vocab=1024)
+    with Model.synthetic(cfg, seed=9, ctx=64) as m:
+        tok = 5
+        for pos in range(4):
+            tok = m.forward_token(tok, pos)
+            lg = m.logits(0)
+            assert np.isfinite(lg).all() and np.abs(lg).max() > 0
