@@ -298,14 +298,29 @@ constexpr int ROUTER_RV = 6;    // float4 per lane per operand in flight
 constexpr int ROUTER_ROWS = 2;  // input rows per block (blockIdx.y = row group)
 
 __global__ void __launch_bounds__(256) router_kernel(const RouterParams r) {
-    pdl_wait();
-    pdl_trigger();
     __shared__ bool last;
     __shared__ float part[8];
     __shared__ int cnt[256], jstart[257], pstart[257];
     __shared__ int ssel[ROUTER_MAX_PAIRS], sorted[ROUTER_MAX_PAIRS];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int P = r.M * r.K;
+    // R does not depend on earlier kernels: when a quarter of D is one pass of
+    // the lanes (D <= 3072), this lane's part of its expert row is loaded
+    // before the dependency wait, once for all rows of the block
+    const int n4p = r.D >> 2, ep = blockIdx.x * 2 + (warp >> 2), qp = warp & 3;
+    const bool rpre_on = !r.sel_in && (r.D & 3) == 0 && ep < r.E && (n4p + 3) / 4 <= 32 * ROUTER_RV;
+    float4 rpre[ROUTER_RV];
+    if (rpre_on) {
+        const int i0 = n4p * qp / 4, i1 = n4p * (qp + 1) / 4;
+        const float4 *r4 = reinterpret_cast<const float4 *>(r.R + (int64_t)ep * r.D);
+#pragma unroll
+        for (int j = 0; j < ROUTER_RV; ++j) {
+            const int i = i0 + lane + 32 * j;
+            rpre[j] = i < i1 ? r4[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+    }
+    pdl_wait();
+    pdl_trigger();
     if (!r.sel_in) {
         const int e = blockIdx.x * 2 + (warp >> 2), q = warp & 3;
         const bool vec = (r.D & 3) == 0;
@@ -355,7 +370,7 @@ __global__ void __launch_bounds__(256) router_kernel(const RouterParams r) {
 #pragma unroll
                         for (int j = 0; j < ROUTER_RV; ++j) {
                             const int i = base + 32 * j;
-                            rv[j] = i < i1 ? r4[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+                            rv[j] = rpre_on ? rpre[j] : (i < i1 ? r4[i] : make_float4(0.f, 0.f, 0.f, 0.f));
                             xv[j] = i < i1 ? x4[i] : make_float4(0.f, 0.f, 0.f, 0.f);
                         }
                         if (fused) {
