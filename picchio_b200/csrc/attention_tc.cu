@@ -15,7 +15,14 @@
 // per warp (running max and sum per head); the four warps' (max, sum, O) are
 // merged with the sink in shared memory, as the span merge of the one-row
 // kernel does (picchio.c:586-596).
+//
+// With few rows the positions are also split over CTAs (blockIdx.z: spans of
+// 512 positions, two tiles per warp): each span's CTA writes its (max, sum,
+// O) per head and the last one (atomic ticket) merges the spans with the sink.
 #include <cuda_bf16.h>
+
+#include <algorithm>
+#include <cstdlib>
 
 #include "kernels.h"
 #include "launch.cuh"
@@ -26,6 +33,7 @@ namespace pc {
 namespace {
 
 constexpr int AT_WARPS = 4, AT_TILE = 64, AT_HD = 64, AT_G = 8;
+constexpr int AT_SPAN = AT_WARPS * 2 * AT_TILE;    // positions per CTA when split (512)
 constexpr int AT_TILE_BYTES = AT_TILE * AT_HD * 2;  // 8 KB: 64 positions x 128 bytes
 constexpr int AT_STAGE = 2 * AT_TILE_BYTES;         // K and V of one tile
 constexpr int AT_MERGE = AT_WARPS * AT_G * (AT_HD + 2) * 4;
@@ -87,16 +95,22 @@ __global__ void __launch_bounds__(AT_WARPS * 32) attn_tc_kernel(const AttnParams
         if (start < 0) start = 0;
     }
     const int64_t cache0 = (int64_t)a.row_seq[m] * a.seq_stride + kh * AT_HD;
-    const int ntiles = (end - start + AT_TILE) / AT_TILE;
+    // this CTA's positions [r0, r1]: the whole row, or span blockIdx.z
+    const int split = gridDim.z > 1, sp = blockIdx.z;
+    const int nsp = split ? (end - start + AT_SPAN) / AT_SPAN : 1;
+    if (sp >= nsp) return;  // uniform: spans past the row's positions
+    const int r0 = start + sp * AT_SPAN;
+    const int r1 = split ? min(end, r0 + AT_SPAN - 1) : end;
+    const int ntiles = (r1 - r0 + AT_TILE) / AT_TILE;
     const int nloc = ntiles > warp ? (ntiles - warp + AT_WARPS - 1) / AT_WARPS : 0;
     uint8_t *wsm = at_smem + warp * 2 * AT_STAGE;
 
     auto issue = [&](int i) {  // this warp's i-th tile into stage i % 2
-        const int p0 = start + AT_TILE * (warp + AT_WARPS * i);
+        const int p0 = r0 + AT_TILE * (warp + AT_WARPS * i);
         uint8_t *ks = wsm + (i & 1) * AT_STAGE, *vs = ks + AT_TILE_BYTES;
         for (int c = lane; c < AT_TILE * 8; c += 32) {
             const int row = c >> 3, ch = c & 7, p = p0 + row;
-            const bool ok = p <= end;
+            const bool ok = p <= r1;
             const int64_t off = cache0 + (int64_t)(ok ? p : start) * kvd + ch * 8;
             cp_async16_zfill(ks + at_off(row, ch), Kc + off, ok ? 16 : 0);
             cp_async16_zfill(vs + at_off(row, ch), Vc + off, ok ? 16 : 0);
@@ -129,7 +143,7 @@ __global__ void __launch_bounds__(AT_WARPS * 32) attn_tc_kernel(const AttnParams
         cp_async_wait<1>();
         __syncwarp();
         const uint32_t ks = smem_u32(wsm + (i & 1) * AT_STAGE), vs = ks + AT_TILE_BYTES;
-        const int p0 = start + AT_TILE * (warp + AT_WARPS * i);
+        const int p0 = r0 + AT_TILE * (warp + AT_WARPS * i);
         // S = Q K^T: n-tile nt = positions 8 nt .. 8 nt + 7
         float s[8][4];
 #pragma unroll
@@ -153,13 +167,13 @@ __global__ void __launch_bounds__(AT_WARPS * 32) attn_tc_kernel(const AttnParams
 #pragma unroll
             for (int j = 0; j < 2; ++j) {
                 const int p = p0 + nt * 8 + 2 * t + j;
-                const float v = p <= end ? __fmul_rn(s[nt][j], scale) : -INFINITY;
+                const float v = p <= r1 ? __fmul_rn(s[nt][j], scale) : -INFINITY;
                 s[nt][j] = v;
                 tmax = fmaxf(tmax, v);
             }
         tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 1));
         tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 2));
-        const float mnew = fmaxf(mrun, tmax);  // finite: position p0 <= end is in the tile
+        const float mnew = fmaxf(mrun, tmax);  // finite: position p0 <= r1 is in the tile
         const float corr = expf(__fsub_rn(mrun, mnew));
         float psum = 0.0f;
 #pragma unroll
@@ -213,20 +227,77 @@ __global__ void __launch_bounds__(AT_WARPS * 32) attn_tc_kernel(const AttnParams
         mw[2 + nt * 8 + 2 * t + 1] = o[nt][1];
     }
     __syncthreads();
+    constexpr int WREC = AT_G * (AT_HD + 2);
+    if (nsp == 1) {
+        for (int idx = threadIdx.x; idx < AT_G * AT_HD; idx += AT_WARPS * 32) {
+            const int gg = idx / AT_HD, d = idx % AT_HD, h = kh * AT_G + gg;
+            float M = a.sinks ? a.sinks[h] : -INFINITY;
+#pragma unroll
+            for (int w = 0; w < AT_WARPS; ++w) M = fmaxf(M, mer[w * WREC + gg * (AT_HD + 2)]);
+            float L = a.sinks ? expf(__fsub_rn(a.sinks[h], M)) : 0.0f;
+            float O = 0.0f;
+#pragma unroll
+            for (int w = 0; w < AT_WARPS; ++w) {
+                const float *rec = mer + w * WREC + gg * (AT_HD + 2);
+                if (rec[1] != 0.0f) {
+                    const float f = expf(__fsub_rn(rec[0], M));
+                    L = __fmaf_rn(rec[1], f, L);
+                    O = __fmaf_rn(rec[2 + d], f, O);
+                }
+            }
+            a.out[(int64_t)m * a.H * AT_HD + h * AT_HD + d] = __fdiv_rn(O, L);
+        }
+        return;
+    }
+    // this span's (max, sum, O) per head, without the sink
+    const int stride = AT_HD + 2;
     for (int idx = threadIdx.x; idx < AT_G * AT_HD; idx += AT_WARPS * 32) {
         const int gg = idx / AT_HD, d = idx % AT_HD, h = kh * AT_G + gg;
-        float M = a.sinks ? a.sinks[h] : -INFINITY;
+        float M = -INFINITY;
 #pragma unroll
-        for (int w = 0; w < AT_WARPS; ++w) M = fmaxf(M, mer[w * AT_G * (AT_HD + 2) + gg * (AT_HD + 2)]);
-        float L = a.sinks ? expf(__fsub_rn(a.sinks[h], M)) : 0.0f;
-        float O = 0.0f;
+        for (int w = 0; w < AT_WARPS; ++w) M = fmaxf(M, mer[w * WREC + gg * (AT_HD + 2)]);
+        float L = 0.0f, O = 0.0f;
 #pragma unroll
         for (int w = 0; w < AT_WARPS; ++w) {
-            const float *rec = mer + w * AT_G * (AT_HD + 2) + gg * (AT_HD + 2);
+            const float *rec = mer + w * WREC + gg * (AT_HD + 2);
             if (rec[1] != 0.0f) {
                 const float f = expf(__fsub_rn(rec[0], M));
                 L = __fmaf_rn(rec[1], f, L);
                 O = __fmaf_rn(rec[2 + d], f, O);
+            }
+        }
+        float *out = a.part + (((int64_t)m * a.H + h) * a.nsplit + sp) * stride;
+        out[2 + d] = O;
+        if (d == 0) {
+            out[0] = M;
+            out[1] = L;
+        }
+    }
+    __threadfence();
+    __syncthreads();
+    __shared__ bool lastf;
+    if (threadIdx.x == 0) {
+        unsigned *c = a.counter + m * a.KVH + kh;
+        lastf = atomicAdd(c, 1u) == (unsigned)(nsp - 1);
+        if (lastf) *c = 0u;
+    }
+    __syncthreads();
+    if (!lastf) return;
+    __threadfence();
+    // merge the spans with the sink (picchio.c:586-596)
+    for (int idx = threadIdx.x; idx < AT_G * AT_HD; idx += AT_WARPS * 32) {
+        const int gg = idx / AT_HD, d = idx % AT_HD, h = kh * AT_G + gg;
+        const float *rec0 = a.part + (((int64_t)m * a.H + h) * a.nsplit) * stride;
+        float M = a.sinks ? a.sinks[h] : -INFINITY;
+        for (int k = 0; k < nsp; ++k) M = fmaxf(M, __ldcg(rec0 + k * stride));
+        float L = a.sinks ? expf(__fsub_rn(a.sinks[h], M)) : 0.0f;
+        float O = 0.0f;
+        for (int k = 0; k < nsp; ++k) {
+            const float l = __ldcg(rec0 + k * stride + 1);
+            if (l != 0.0f) {
+                const float f = expf(__fsub_rn(__ldcg(rec0 + k * stride), M));
+                L = __fmaf_rn(l, f, L);
+                O = __fmaf_rn(__ldcg(rec0 + k * stride + 2 + d), f, O);
             }
         }
         a.out[(int64_t)m * a.H * AT_HD + h * AT_HD + d] = __fdiv_rn(O, L);
@@ -236,7 +307,9 @@ __global__ void __launch_bounds__(AT_WARPS * 32) attn_tc_kernel(const AttnParams
 }  // namespace
 
 bool attention_tc_ok(const AttnParams &a) {
-    return a.kv_bf16 && a.hd == AT_HD && a.H == a.KVH * AT_G && a.M >= ATTN_TC_MIN_ROWS;
+    const char *v = getenv("PICCHIO_ATTN_TC");  // 0: the one-row kernel for every step
+    const bool off = v && v[0] == '0';
+    return !off && a.kv_bf16 && a.hd == AT_HD && a.H == a.KVH * AT_G;
 }
 
 cudaError_t attention_tc_configure() {
@@ -244,7 +317,10 @@ cudaError_t attention_tc_configure() {
 }
 
 cudaError_t launch_attention_tc(const AttnParams &a, cudaStream_t st) {
-    return launch_k(attn_tc_kernel, dim3(a.M, a.KVH), dim3(AT_WARPS * 32), AT_SMEM, st, a);
+    // few rows: the positions split over CTAs too, in spans of 512 (the
+    // partial records hold a.nsplit spans of 256, so at most that many)
+    const int nz = a.M >= ATTN_TC_MIN_ROWS ? 1 : std::max(1, (a.nsplit + 1) / 2);
+    return launch_k(attn_tc_kernel, dim3(a.M, a.KVH, nz), dim3(AT_WARPS * 32), AT_SMEM, st, a);
 }
 
 }  // namespace pc

@@ -37,9 +37,10 @@ struct AttnParams {
 constexpr int ATTN_SPLIT = 256;
 // gqa_attention's score / softmax-with-sink / P.V part (picchio.c:556-607).
 cudaError_t launch_attention(const AttnParams &a, cudaStream_t st);
-// The tensor-core form (attention_tc.cu) for steps of ATTN_TC_MIN_ROWS rows
-// or more with a bf16 KV cache, head size 64 and 8 query heads per KV head;
-// launch_attention picks it when attention_tc_ok.
+// The tensor-core form (attention_tc.cu) for a bf16 KV cache, head size 64
+// and 8 query heads per KV head; launch_attention picks it when
+// attention_tc_ok.  Below ATTN_TC_MIN_ROWS rows it also splits the positions
+// over CTAs (spans of 512).
 constexpr int ATTN_TC_MIN_ROWS = 16;
 bool attention_tc_ok(const AttnParams &a);
 cudaError_t attention_tc_configure();

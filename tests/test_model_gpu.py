@@ -433,9 +433,10 @@ def _gptoss_heads_model(**kw):
 
 def test_tensor_core_attention_batch_matches_single_rows():
     """32 sequences at 600 cached positions (window layer and full layer):
-    the batch step runs the tensor-core attention (Q and P as bf16 hi + lo
-    halves against the bf16 cache); rows 0, 7 and 31 equal the same
-    sequences decoded alone (the fp32 one-row kernel): same next id, logits
+    the batch step runs the tensor-core attention one CTA per row (Q and P as
+    bf16 hi + lo halves against the bf16 cache); rows 0, 7 and 31 equal the
+    same sequences decoded alone (the span-split form for one row, itself
+    checked against the fp32 one-row kernel below): same next id, logits
     within 1e-3."""
     B, n = 32, 600
     toks = [(7 * s + 3) % 1000 for s in range(B)]
@@ -481,3 +482,20 @@ def test_synthetic_model_with_wide_attention_is_finite():
             tok = m.forward_token(tok, pos)
             lg = m.logits(0)
             assert np.isfinite(lg).all() and np.abs(lg).max() > 0
+
+
+def test_tensor_core_attention_one_row_matches_one_row_kernel(monkeypatch):
+    """Batch-1 decode at position 600 with a bf16 cache: the tensor-core
+    attention (positions split in spans of 512, merged by the last CTA) gives
+    the one-row fp32 kernel's next id and logits within 1e-4."""
+    n = 600
+    out = {}
+    for tc in ("0", "1"):
+        monkeypatch.setenv("PICCHIO_ATTN_TC", tc)
+        with _gptoss_heads_model(ctx=n + 8) as m:
+            m.kv_fill_synthetic(n, seq=0, seed=77)
+            t = m.forward_token(9, n)
+            t2 = m.forward_token(t, n + 1)
+            out[tc] = (t, t2, m.logits(0))
+    assert out["0"][:2] == out["1"][:2]
+    assert rel_l2(out["1"][2], out["0"][2]) < 1e-4
