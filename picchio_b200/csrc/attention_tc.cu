@@ -77,10 +77,12 @@ __device__ __forceinline__ void split2(float x0, float x1, uint32_t &hi, uint32_
 // byte offset of 16-byte chunk ch of tile row `row` (128-byte rows, swizzled)
 __device__ __forceinline__ uint32_t at_off(int row, int ch) { return row * 128 + ((ch ^ (row & 7)) << 4); }
 
+// FEW: the few-row form (span split over blockIdx.z, early tile requests for
+// one row); the many-row instance compiles without either.
+template <bool FEW>
 __global__ void __launch_bounds__(AT_WARPS * 32) attn_tc_kernel(const AttnParams a) {
     extern __shared__ __align__(128) uint8_t at_smem[];
     pdl_trigger();
-    pdl_wait();  // q and this step's K/V rows come from the q/k/v kernel
     const int m = blockIdx.x, kh = blockIdx.y;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
     const __nv_bfloat16 *Kc = reinterpret_cast<const __nv_bfloat16 *>(a.kc);
@@ -96,7 +98,7 @@ __global__ void __launch_bounds__(AT_WARPS * 32) attn_tc_kernel(const AttnParams
     }
     const int64_t cache0 = (int64_t)a.row_seq[m] * a.seq_stride + kh * AT_HD;
     // this CTA's positions [r0, r1]: the whole row, or span blockIdx.z
-    const int split = gridDim.z > 1, sp = blockIdx.z;
+    const int split = FEW && gridDim.z > 1, sp = FEW ? blockIdx.z : 0;
     const int nsp = split ? (end - start + AT_SPAN) / AT_SPAN : 1;
     if (sp >= nsp) return;  // uniform: spans past the row's positions
     const int r0 = start + sp * AT_SPAN;
@@ -117,7 +119,15 @@ __global__ void __launch_bounds__(AT_WARPS * 32) attn_tc_kernel(const AttnParams
         }
         cp_async_commit();
     };
-    if (nloc > 0) issue(0);
+    // q and this step's K/V row come from the q/k/v kernel; with one row,
+    // this warp's first tiles that end before the row's position (rows of
+    // earlier steps) are requested before waiting for it
+    int issued = 0;
+    while (FEW && a.M == 1 && issued < 2 && issued < nloc &&
+           min(r0 + AT_TILE * (warp + AT_WARPS * issued) + AT_TILE - 1, r1) < pos)
+        issue(issued++);
+    pdl_wait();
+    if (issued == 0 && nloc > 0) issue(issued++);
 
     // Q of head g (A rows 0-7), dims 16 ks + 2t (+1) and 16 ks + 8 + 2t (+1)
     const float *q = a.q + (int64_t)m * a.H * AT_HD + (int64_t)(kh * AT_G + g) * AT_HD;
@@ -138,7 +148,7 @@ __global__ void __launch_bounds__(AT_WARPS * 32) attn_tc_kernel(const AttnParams
         for (int j = 0; j < 4; ++j) o[nt][j] = 0.0f;
 
     for (int i = 0; i < nloc; ++i) {
-        if (i + 1 < nloc) issue(i + 1);
+        if (i + 1 < nloc && i + 1 >= issued) issue(i + 1);
         else cp_async_commit();
         cp_async_wait<1>();
         __syncwarp();
@@ -228,7 +238,7 @@ __global__ void __launch_bounds__(AT_WARPS * 32) attn_tc_kernel(const AttnParams
     }
     __syncthreads();
     constexpr int WREC = AT_G * (AT_HD + 2);
-    if (nsp == 1) {
+    if (!FEW || nsp == 1) {
         for (int idx = threadIdx.x; idx < AT_G * AT_HD; idx += AT_WARPS * 32) {
             const int gg = idx / AT_HD, d = idx % AT_HD, h = kh * AT_G + gg;
             float M = a.sinks ? a.sinks[h] : -INFINITY;
@@ -313,14 +323,19 @@ bool attention_tc_ok(const AttnParams &a) {
 }
 
 cudaError_t attention_tc_configure() {
-    return cudaFuncSetAttribute(attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, AT_SMEM);
+    cudaError_t e = cudaFuncSetAttribute(attn_tc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, AT_SMEM);
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(attn_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, AT_SMEM);
+    return e;
 }
 
 cudaError_t launch_attention_tc(const AttnParams &a, cudaStream_t st) {
     // few rows: the positions split over CTAs too, in spans of 512 (the
     // partial records hold a.nsplit spans of 256, so at most that many)
-    const int nz = a.M >= ATTN_TC_MIN_ROWS ? 1 : std::max(1, (a.nsplit + 1) / 2);
-    return launch_k(attn_tc_kernel, dim3(a.M, a.KVH, nz), dim3(AT_WARPS * 32), AT_SMEM, st, a);
+    if (a.M >= ATTN_TC_MIN_ROWS)
+        return launch_k(attn_tc_kernel<false>, dim3(a.M, a.KVH), dim3(AT_WARPS * 32), AT_SMEM, st, a);
+    const int nz = std::max(1, (a.nsplit + 1) / 2);
+    return launch_k(attn_tc_kernel<true>, dim3(a.M, a.KVH, nz), dim3(AT_WARPS * 32), AT_SMEM, st, a);
 }
 
 }  // namespace pc
