@@ -444,17 +444,19 @@ __global__ void __launch_bounds__(256) router_kernel(const RouterParams r) {
 // (row, expert) dot exactly as router_kernel does (four quarters of D, lanes
 // strided by 32 float4 with four component sums, the same shuffle tree, the
 // quarters added as (q0 + q1) + (q2 + q3)), so the logits are bit-identical;
-// the next quarter's R loads are in flight while a quarter is summed.  Each
-// block takes the top-k of its own rows; the last block (ticket) builds the
-// job tables.  D % 4 == 0 and one 32 x ROUTER_RV float4 pass per quarter
+// the next quarter's R loads are in flight while a quarter is summed.  Below
+// 256 rows the experts are split over blockIdx.y (ROUTER_EPB per block); the
+// last expert block of a row block (ticket) takes those rows' top-k, and the
+// last row block the job tables.  D % 4 == 0 and one 32 x ROUTER_RV float4 pass per quarter
 // (D <= 3072).
-constexpr int ROUTER_RB_MIN_ROWS = 256;  // from this many rows the row-block form is used
+constexpr int ROUTER_RB_MIN_ROWS = 16;  // from this many rows the row-block form is used
+constexpr int ROUTER_EPB = 16;          // experts per block of the row-block form (blockIdx.y)
 
 // Row-block router helpers: R of task t ((expert warp + 8 (t / 4), quarter
 // t % 4)) into registers, and the task's dots for the block's RB rows.
-__device__ __forceinline__ void rr_load(const RouterParams &r, int n4, int warp, int lane, int t,
+__device__ __forceinline__ void rr_load(const RouterParams &r, int n4, int ebase, int warp, int lane, int t,
                                         float4 (&rv)[ROUTER_RV]) {
-    const int e = warp + 8 * (t >> 2), q = t & 3;
+    const int e = ebase + warp + 8 * (t >> 2), q = t & 3;
     const int i0 = n4 * q / 4, i1 = n4 * (q + 1) / 4;
     const float4 *r4 = reinterpret_cast<const float4 *>(r.R + (int64_t)e * r.D);
 #pragma unroll
@@ -465,10 +467,10 @@ __device__ __forceinline__ void rr_load(const RouterParams &r, int n4, int warp,
 }
 
 template <int RB>
-__device__ __forceinline__ void rr_task(const RouterParams &r, const float4 *xn4, int n4, int warp, int lane, int t,
-                                        int nr, int m0, const float4 (&rv)[ROUTER_RV], float (&p0)[RB],
-                                        float (&a01)[RB], float (&p2)[RB], float *lgs) {
-    const int e = warp + 8 * (t >> 2), q = t & 3;
+__device__ __forceinline__ void rr_task(const RouterParams &r, const float4 *xn4, int n4, int ebase, int warp, int lane,
+                                        int t, int nr, int m0, const float4 (&rv)[ROUTER_RV], float (&p0)[RB],
+                                        float (&a01)[RB], float (&p2)[RB]) {
+    const int e = ebase + warp + 8 * (t >> 2), q = t & 3;
     const int i0 = n4 * q / 4, i1 = n4 * (q + 1) / 4;
 #pragma unroll
     for (int rr = 0; rr < RB; ++rr) {
@@ -495,7 +497,6 @@ __device__ __forceinline__ void rr_task(const RouterParams &r, const float4 *xn4
         } else if (lane == 0 && rr < nr) {
             float lv = __fadd_rn(a01[rr], __fadd_rn(p2[rr], v));
             if (r.bias) lv = r.bias_first ? __fadd_rn(r.bias[e], lv) : __fadd_rn(lv, r.bias[e]);
-            lgs[rr * 256 + e] = lv;
             r.logits[(int64_t)(m0 + rr) * r.E + e] = lv;
         }
     }
@@ -505,8 +506,7 @@ template <int RB>
 __global__ void __launch_bounds__(256) router_rows_kernel(const RouterParams r) {
     extern __shared__ float4 rsm4[];
     float4 *xn4 = rsm4;  // [RB][D / 4]
-    __shared__ float lgs[RB][256];
-    __shared__ bool last;
+    __shared__ bool last, rowlast;
     __shared__ int cnt[256], jstart[257], pstart[257];
     __shared__ int ssel[ROUTER_MAX_PAIRS], sorted[ROUTER_MAX_PAIRS];
     pdl_wait();
@@ -544,7 +544,7 @@ __global__ void __launch_bounds__(256) router_rows_kernel(const RouterParams r) 
                     const float4 v = make_float4(__fmul_rn(__fmul_rn(hv[j].x, rn), w.x), __fmul_rn(__fmul_rn(hv[j].y, rn), w.y),
                                                  __fmul_rn(__fmul_rn(hv[j].z, rn), w.z), __fmul_rn(__fmul_rn(hv[j].w, rn), w.w));
                     dst[i] = v;
-                    o4[i] = v;
+                    if (blockIdx.y == 0) o4[i] = v;
                 }
             }
         } else {
@@ -553,21 +553,36 @@ __global__ void __launch_bounds__(256) router_rows_kernel(const RouterParams r) 
         }
     }
     __syncthreads();
-    // (expert, quarter) tasks of this warp, R of the next task in flight
-    const int ne = (r.E - warp + 7) / 8, T = 4 * max(ne, 0);
+    // (expert, quarter) tasks of this warp over this block's experts
+    // [ebase, ebase + ROUTER_EPB), R of the next task in flight
+    const int epb = (r.E + gridDim.y - 1) / gridDim.y;
+    const int ebase = blockIdx.y * epb, eend = min(r.E, ebase + epb);
+    const int ne = (eend - ebase - warp + 7) / 8, T = 4 * max(ne, 0);
     float4 ra[ROUTER_RV], rb[ROUTER_RV];
     float p0[RB], a01[RB], p2[RB];
-    if (T > 0) rr_load(r, n4, warp, lane, 0, ra);
+    if (T > 0) rr_load(r, n4, ebase, warp, lane, 0, ra);
     for (int t = 0; t < T; t += 2) {
-        if (t + 1 < T) rr_load(r, n4, warp, lane, t + 1, rb);
-        rr_task<RB>(r, xn4, n4, warp, lane, t, nr, m0, ra, p0, a01, p2, &lgs[0][0]);
+        if (t + 1 < T) rr_load(r, n4, ebase, warp, lane, t + 1, rb);
+        rr_task<RB>(r, xn4, n4, ebase, warp, lane, t, nr, m0, ra, p0, a01, p2);
         if (t + 1 < T) {
-            if (t + 2 < T) rr_load(r, n4, warp, lane, t + 2, ra);
-            rr_task<RB>(r, xn4, n4, warp, lane, t + 1, nr, m0, rb, p0, a01, p2, &lgs[0][0]);
+            if (t + 2 < T) rr_load(r, n4, ebase, warp, lane, t + 2, ra);
+            rr_task<RB>(r, xn4, n4, ebase, warp, lane, t + 1, nr, m0, rb, p0, a01, p2);
         }
     }
+    // the last expert block of this row block takes its rows' top-k
+    __threadfence();
     __syncthreads();
-    for (int rr = warp; rr < nr; rr += 8) router_topk_row<false>(r, lgs[rr], m0 + rr, nullptr);
+    if (tid == 0) {
+        unsigned *c = r.counter + 1 + blockIdx.x;
+        rowlast = atomicAdd(c, 1u) == gridDim.y - 1;
+        if (rowlast) *c = 0u;
+    }
+    __syncthreads();
+    if (!rowlast) return;
+    __threadfence();
+    for (int rr = warp; rr < nr; rr += 8)
+        router_topk_row<true>(r, r.logits + (int64_t)(m0 + rr) * r.E, m0 + rr, nullptr);
+    // ... and the last row block the job tables
     __threadfence();
     __syncthreads();
     if (tid == 0) {
@@ -806,8 +821,10 @@ cudaError_t launch_router(const RouterParams &r, cudaStream_t st) {
     if (r.ln_w && ((r.D & 3) || r.D > 4 * NORM_V4 * NORM_THREADS || !r.h_in || !r.hn_out)) return cudaErrorInvalidValue;
     if (!r.sel_in && r.M >= ROUTER_RB_MIN_ROWS && (r.D & 3) == 0 && r.D <= 4 * 32 * ROUTER_RV * 4 &&
         r.D <= 4 * NORM_V4 * NORM_THREADS) {
-        const int rb = r.M >= 256 ? 4 : 2;  // at least ~64 blocks
-        const dim3 grid((r.M + rb - 1) / rb);
+        // many rows: 4 per block, all experts (enough blocks already); fewer:
+        // 2 rows per block and the experts split ROUTER_EPB per block
+        const int rb = r.M >= 256 ? 4 : 2;
+        const dim3 grid((r.M + rb - 1) / rb, r.M >= 256 ? 1 : (r.E + ROUTER_EPB - 1) / ROUTER_EPB);
         const size_t smem = (size_t)rb * r.D * 4;
         return rb == 4 ? launch_k(router_rows_kernel<4>, grid, dim3(256), smem, st, r)
                        : launch_k(router_rows_kernel<2>, grid, dim3(256), smem, st, r);

@@ -57,7 +57,7 @@ struct RouterParams {
     float *logits;         // [M][E]
     int *sel;              // [M][K]
     float *w;              // [M][K]
-    unsigned *counter;     // zero, self-resetting
+    unsigned *counter;     // zero, self-resetting tickets: [0] the launch, [1 + b] row block b (row-block form)
     const int *sel_in;     // optional given routing [M][K] (skips router + top-k)
     // optional fused input norm: x[m] = rmsnorm(h_in[m], ln_w, eps) computed
     // in every block (exactly as rmsnorm_kernel does), written to hn_out[m]

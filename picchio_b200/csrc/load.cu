@@ -438,7 +438,9 @@ pc_status alloc_runtime(pc_ctx *c) {
     PC_TRY(dalloc(c, 16, (void **)&c->njobs));
     PC_TRY(dalloc(c, sizeof(GemvJob) * GEMV_MAX_JOBS, (void **)&c->jobs_gu));
     PC_TRY(dalloc(c, sizeof(GemvJob) * GEMV_MAX_JOBS, (void **)&c->jobs_dn));
-    PC_TRY(dalloc(c, 16, (void **)&c->router_ctr));
+    // router tickets: [0] the whole launch, [1 + b] row block b of the row-block form
+    PC_TRY(dalloc(c, (size_t)(M + 4) * 4, (void **)&c->router_ctr));
+    PC_CU(cudaMemset(c->router_ctr, 0, (size_t)(M + 4) * 4));
     PC_TRY(dalloc(c, (size_t)M * KVH * 4, (void **)&c->attn_ctr));
     c->attn_max_split = (c->kv_ctx + 255) / 256;
     if (c->attn_max_split > 64)  // the decode attention merges at most 64 spans of 256 positions
