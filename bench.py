@@ -191,10 +191,51 @@ def run_reference(args, world, rank):
 BS64 = 64
 
 
-def bs64_decode(m, ctx0, pos0, steps=16, warmup=3):
+def tiny_e2e(dev, prompt_len=64, steps=32, seed=1234):
+    """BASELINE configs[0] end to end through the C ABI: the tiny seeded model
+    loaded from its container (pc_init), a prompt_len-id prompt (pc_prefill),
+    then `steps` greedy tokens one pc_forward_token call each (host ints in
+    and out), host clock.  The counterpart of cpu_baseline_e2e."""
+    import tempfile
+
+    from picchio_b200 import Model
+    from picchio_b200.synth import SynthConfig, make_model, random_prompt
+    cfg = SynthConfig()
+    with tempfile.TemporaryDirectory() as d:
+        make_model(d, cfg, seed)
+        prompt = random_prompt(prompt_len, cfg.vocab_size, 7)
+        with Model(d, ctx=512, device=dev) as m:
+            m.generate(prompt, steps)  # warm-up: graphs captured
+            t0 = time.perf_counter()
+            tok = m.prefill_tokens(prompt, 0)
+            t1 = time.perf_counter()
+            pos = prompt_len
+            for _ in range(steps):
+                tok = m.forward_token(tok, pos)
+                pos += 1
+            t2 = time.perf_counter()
+    return {"value": steps / (t2 - t1), "unit": "tok/s", "prefill_s": t1 - t0,
+            "sample": f"tiny seeded model (configs[0]), {prompt_len}-id prompt, {steps} greedy tokens through "
+                      f"pc_forward_token, host clock"}
+
+
+def ids_on_one_gpu(cfg, ctx, dev, args, warm_ids, timed_ids):
+    """The bench's greedy decode (warm-up then timed steps from token 1 at
+    position CTX_PREFIX) on one GPU without expert parallelism: True when its
+    ids equal the expert-parallel run's."""
+    from picchio_b200 import Model
+    with Model.synthetic(cfg, seed=2024, ctx=ctx, device=dev, kv_bf16=KV_BF16) as m1:
+        m1.kv_fill_synthetic(CTX_PREFIX)
+        w, _ = m1.generate_device(1, CTX_PREFIX, args.warmup)
+        t, _ = m1.generate_device(w[-1], CTX_PREFIX + args.warmup, args.steps)
+    return w == warm_ids and t == timed_ids
+
+
+def bs64_decode(m, ctx0, pos0, world=1, steps=16, warmup=3):
     """Batch-64 greedy decode (BASELINE metric's bs64 leg): 64 sequences, each
     with a seeded 4096-position KV prefix, one pc_decode_batch call per step
-    (host ints in and out), host clock over the timed steps."""
+    (host ints in and out), host clock over the timed steps, the max over
+    expert-parallel ranks."""
     for s in range(1, BS64):
         m.kv_fill_synthetic(ctx0, seq=s, seed=99 + s)
     toks = [(7 * s + 1) % 1000 for s in range(BS64)]
@@ -202,11 +243,12 @@ def bs64_decode(m, ctx0, pos0, steps=16, warmup=3):
     for _ in range(warmup):
         toks = m.decode_batch(toks, pos)
         pos = [p + 1 for p in pos]
+    barrier(world)
     t0 = time.perf_counter()
     for _ in range(steps):
         toks = m.decode_batch(toks, pos)
         pos = [p + 1 for p in pos]
-    dt = time.perf_counter() - t0
+    dt = allmax(time.perf_counter() - t0, world)
     # per-kernel device time of one more step (CUDA events around every launch)
     m.profile_begin()
     toks = m.decode_batch(toks, pos)
@@ -294,6 +336,86 @@ def moe_micro(dev, iters=20):
     return out
 
 
+def probe(args):
+    """Small repeatable workloads for the ncu captures under profiles/ (not
+    bench values).  --probe decode: a few steps of a GPT-OSS-120B-shaped model
+    with --layers layers, without CUDA graphs (every launch visible on its
+    own); --batch B > 1 makes each step one pc_decode_batch, --prefill N
+    instead encodes N seeded ids in --chunk-position steps.  --probe gemv:
+    pc_qt_matmul on one seeded --rows x --cols matrix, timed.  --probe moe:
+    the configs[1] expert layer (pc_moe_experts) at --rows rows."""
+    import numpy as np
+    import torch
+    from picchio_b200 import FMT_INT4, FMT_INT8, QT, Model, ModelConfig
+    if args.probe == "decode":
+        cfg = ModelConfig.gpt_oss_120b()
+        cfg.n_layers = args.layers
+        if args.prefill > 0:
+            m = Model.synthetic(cfg, seed=1, ctx=args.prefill + 8, use_graphs=False, kv_bf16=True,
+                                prefill_chunk=args.chunk)
+            ids = np.random.default_rng(7).integers(0, cfg.vocab, args.prefill).tolist()
+            print("ok", m.prefill_tokens(ids, 0))
+            return
+        B = args.batch
+        m = Model.synthetic(cfg, seed=1, ctx=CTX_PREFIX + args.steps + 8, use_graphs=False, kv_bf16=True,
+                            max_batch=B)
+        for s in range(B):
+            m.kv_fill_synthetic(CTX_PREFIX, seq=s, seed=7 + s)
+        if B == 1:
+            tok = 1
+            for i in range(args.steps):
+                tok = m.forward_token(tok, CTX_PREFIX + i)
+            print("ok", tok)
+        else:
+            toks = [(3 * s + 1) % 1000 for s in range(B)]
+            for i in range(args.steps):
+                toks = m.decode_batch(toks, [CTX_PREFIX + i] * B)
+            print("ok", toks[:4])
+        return
+    if args.probe == "gemv":
+        O, I = args.rows, args.cols
+        rng = np.random.default_rng(7)
+        if args.int8:
+            q = QT(FMT_INT8, O, I, rng.integers(-127, 128, size=(O, I), dtype=np.int8), np.full(O, 1e-3, np.float32))
+            nbytes = O * I + 4 * O
+        else:
+            ng = (I + args.gs - 1) // args.gs if args.gs else 1
+            q = QT(FMT_INT4, O, I, rng.integers(0, 256, size=(O, (I + 1) // 2), dtype=np.uint8),
+                   np.full(O * ng, 1e-3, np.float32), block_size=args.gs)
+            nbytes = O * ((I + 1) // 2) + 4 * O * ng
+        x = torch.from_numpy(rng.standard_normal((args.S, I)).astype(np.float32)).cuda()
+        for _ in range(3):
+            q.matmul(x)
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(args.iters):
+            q.matmul(x)
+        b.record()
+        torch.cuda.synchronize()
+        us = a.elapsed_time(b) * 1e3 / args.iters
+        print(f"rows={O} cols={I} {'int8' if args.int8 else f'int4 gs{args.gs}'} S={args.S}: "
+              f"{us:.2f} us/launch, {nbytes / us / 1e3:.0f} GB/s (weight + scale bytes)")
+        return
+    # moe: the single-layer expert microbench of configs[1] at one row count
+    cfg = ModelConfig(hidden=2880, n_layers=1, n_heads=64, n_kv_heads=8, head_dim=64, n_experts=32, topk=4,
+                      intermediate=2880, vocab=1024)
+    M = args.rows
+    m = Model.synthetic(cfg, seed=5, ctx=64, max_batch=max(M, 1))
+    rng = np.random.default_rng(11)
+    sel = np.stack([rng.choice(32, 4, replace=False) for _ in range(M)]).astype(np.int32)
+    w = rng.random((M, 4)).astype(np.float32)
+    w /= w.sum(1, keepdims=True)
+    x = torch.from_numpy(rng.standard_normal((M, cfg.hidden)).astype(np.float32)).cuda()
+    s_d, w_d = torch.from_numpy(sel).cuda(), torch.from_numpy(w).cuda()
+    out = None
+    for _ in range(args.iters):
+        out = m.moe_experts(x, s_d, w_d, 0)
+    torch.cuda.synchronize()
+    print("ok", float(out.abs().sum()))
+    m.close()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -303,7 +425,22 @@ def main():
     ap.add_argument("--layers", type=int, default=36, help="fewer layers: quick checks only, not a bench value")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-extra", action="store_true", help="skip the bs64 and expert-microbench side measurements")
+    ap.add_argument("--probe", choices=["decode", "gemv", "moe"], help="profiling workload only (no bench line)")
+    ap.add_argument("--batch", type=int, default=1, help="--probe decode: sequences per step")
+    ap.add_argument("--prefill", type=int, default=0, help="--probe decode: ids to encode instead of decoding")
+    ap.add_argument("--chunk", type=int, default=64, help="--probe decode: positions per prefill step")
+    ap.add_argument("--rows", type=int, default=368640, help="--probe gemv: matrix rows; --probe moe: token rows")
+    ap.add_argument("--cols", type=int, default=2880, help="--probe gemv: matrix columns")
+    ap.add_argument("--gs", type=int, default=32, help="--probe gemv: INT4 group size (0 = per-row scale)")
+    ap.add_argument("--int8", action="store_true", help="--probe gemv: an INT8 matrix")
+    ap.add_argument("--S", type=int, default=1, help="--probe gemv: input rows")
+    ap.add_argument("--iters", type=int, default=20, help="--probe gemv/moe: calls")
     args = ap.parse_args()
+    if args.probe:
+        import torch
+        torch.cuda.set_device(0)
+        probe(args)
+        return
     args.warmup = max(args.warmup, 3)
     world, rank, local = dist_setup()
     if args.impl == "reference":
@@ -320,10 +457,11 @@ def main():
     cfg.n_layers = args.layers
     ctx = CTX_PREFIX + args.warmup + 2 * args.steps + 64
     t0 = time.time()
-    extra = world == 1 and not args.no_extra
+    extra = not args.no_extra          # bs64 decode at every N
+    single_extra = extra and world == 1  # prefill and the expert microbench: one GPU only
     m = Model.synthetic(cfg, seed=2024, ctx=ctx, device=local, ep_rank=rank, ep_size=world, nccl_id=nid,
                         kv_bf16=KV_BF16, max_batch=BS64 if extra else 1,
-                        prefill_chunk=PREFILL_CHUNK if extra else 64)
+                        prefill_chunk=PREFILL_CHUNK if single_extra else 64)
     t_init = time.time() - t0
     m.kv_fill_synthetic(CTX_PREFIX)
     clk = Clocks(local)
@@ -332,9 +470,9 @@ def main():
     pos = CTX_PREFIX
     tok = 1
     # warm-up (graph capture + first replays)
-    ids, _ = m.generate_device(tok, pos, args.warmup)
+    warm_ids, _ = m.generate_device(tok, pos, args.warmup)
     pos += args.warmup
-    tok = ids[-1]
+    tok = warm_ids[-1]
     barrier(world)
     torch.cuda.synchronize()
     l0 = m.launches
@@ -343,6 +481,7 @@ def main():
     torch.cuda.synchronize()
     barrier(world)
     launches = m.launches - l0
+    timed_ids = ids
     pos += args.steps
     tok = ids[-1]
     dev_ms = allmax(dev_ms, world)
@@ -362,10 +501,17 @@ def main():
 
     # kernel timing for the roofline: profiling steps, each captured into a
     # one-off graph with CUDA events around every launch (device time only)
+    # Under expert parallelism a rank's expert launches stream only the
+    # routed experts it owns: count them from each profiled step's routing.
+    E = cfg.n_experts
+    e_lo, e_hi = E * rank // world, E * (rank + 1) // world
+    local_experts = 0
     m.profile_begin()
     for _ in range(3):
         tok = m.forward_token(tok, pos)
         pos += 1
+        sel = m.routing()  # [layers, 1, topk]
+        local_experts += sum(len({int(e) for e in sel[l, 0] if e_lo <= e < e_hi}) for l in range(cfg.n_layers))
     prof = m.profile_end()
     hbm, peak_kind = peaks()
     K = cfg.topk
@@ -373,17 +519,19 @@ def main():
     # tile bytes (nibbles + interleaved group scales) + bias, per expert
     dn_bytes = (cfg.hidden // 16) * (cfg.intermediate // 64) * (512 + (64 // gs) * 64) + 4 * cfg.hidden
     gu_bytes = ((2 * cfg.intermediate) // 16) * (cfg.hidden // 64) * (512 + (64 // gs) * 64) + 4 * 2 * cfg.intermediate
-    n_local = K  # experts a bs1 token touches (all resident on one GPU)
     gu_ms, gu_n = prof.get("expert_gate_up", (0.0, 0))
     dn_ms, dn_n = prof.get("expert_down", (0.0, 0))
-    achieved = (n_local * gu_bytes) / (gu_ms / gu_n / 1e3) / 1e9 if gu_n else None
-    achieved_pair = (n_local * (gu_bytes + dn_bytes)) / ((gu_ms / gu_n + dn_ms / dn_n) / 1e3) / 1e9 if gu_n and dn_n else None
-    traffic = traffic_from_profiles()
+    # algorithmic bytes of all profiled gate_up launches / their summed device time
+    achieved = local_experts * gu_bytes / (gu_ms / 1e3) / 1e9 if gu_n and local_experts else None
+    achieved_pair = (local_experts * (gu_bytes + dn_bytes)) / ((gu_ms + dn_ms) / 1e3) / 1e9 \
+        if gu_n and dn_n and local_experts else None
+    traffic = traffic_from_profiles() if world == 1 else None
+    bytes_per_launch = local_experts * gu_bytes / gu_n if gu_n else None
 
     line = {
         "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": dev_ms / args.steps, "higher_is_better": True,
-        "scaling": "strong" if world > 1 else "weak", "vs_baseline": None,
+        "scaling": "strong", "vs_baseline": None,
         "dtype": "int4/int8 weights; s8 tensor-core MMA on 3-digit int8 splits of the fp32 activations "
                  "(exact s32 group sums), fp32 accumulate",
         "data": "synthetic (seeded random-init weights generated on device; synthetic 4096-position KV prefix)",
@@ -396,25 +544,39 @@ def main():
                    "init_s": round(t_init, 2)},
         "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": 8, "d2h_bytes_per_step": 8},
         "gpu_launches": launches,
-        "roofline": {"bound": "hbm", "kernel": "expert gate_up GEMV (4 experts, INT4 gs32)",
+        "roofline": {"bound": "hbm",
+                     "kernel": "expert gate_up GEMV (the routed experts this rank owns, INT4 gs32)",
                      "achieved": achieved, "peak": hbm, "unit": "GB/s",
                      "frac": (achieved / hbm) if achieved else None, "peak_kind": f"{peak_kind} hbm_gbs",
                      "traffic": traffic,
-                     "algorithmic_bytes_per_launch": n_local * gu_bytes,
+                     "algorithmic_bytes_per_launch": bytes_per_launch,
+                     "local_experts_per_launch": local_experts / gu_n if gu_n else None,
                      "gate_up_plus_down_gbs": achieved_pair},
         "kernel_ms": {k: v[0] / v[1] for k, v in prof.items()},
         "clocks": clk.summary(),
     }
-    if extra:
+    if single_extra:
         line["prefill"] = prefill_bench(m, cfg.vocab)
-        line["bs64"] = bs64_decode(m, CTX_PREFIX, pos)
-        m.close()
+    if extra:
+        line["bs64"] = bs64_decode(m, CTX_PREFIX, pos, world)
+    m.close()
+    if single_extra:
         line["moe_micro"] = moe_micro(local)
+    if world > 1:
+        # rank 0 replays the timed decode on one GPU (the same seeded model,
+        # no expert parallelism) and compares the greedy ids
+        barrier(world)
+        if rank == 0:
+            line["ids_match_1gpu"] = ids_on_one_gpu(cfg, ctx, local, args, warm_ids, timed_ids)
+        barrier(world)
+    if rank == 0 and world == 1 and not args.no_extra:
+        line["tiny_e2e"] = tiny_e2e(local)
     if rank == 0 and world == 1 and not args.no_cpu:
         from oracle import cpu_baseline
         r = cpu_baseline.measure(ctx=CTX_PREFIX)
         line["cpu_baseline"] = {"value": r["tok_s"], "unit": "tok/s", "cores": r["cores"], "kind": r["kind"],
                                 "sample": r["sample"]}
+        line["cpu_baseline_e2e"] = cpu_baseline.measure_e2e()
     m.close()
     if rank == 0:
         print(json.dumps(line), flush=True)

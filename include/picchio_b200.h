@@ -197,6 +197,14 @@ pc_status pc_moe_layer(pc_ctx *ctx, int layer, const float *x_dev, float *out_de
 pc_status pc_moe_experts(pc_ctx *ctx, int layer, const float *x_dev, const int *sel_dev,
                          const float *w_dev, int M, float *out_dev);
 
+/* Router selections of the last step (decode step, batch, prefill chunk or
+ * MoE call): expert ids [n_layers][rows][topk] in selection order, the
+ * top-k of moe_forward (picchio.c:1326-1340) that the reference dumps as
+ * layerN.top_indices.  *rows receives the step's row count; cap (ids) must
+ * hold n_layers * rows * topk, else PC_ERR_RANGE.  Every expert-parallel rank
+ * routes identically. */
+pc_status pc_get_routing(pc_ctx *ctx, int *expert_ids, int cap, int *rows);
+
 /* Stage tensors of the last pc_forward_token, under the names the reference's
  * ORACLE_DIR dump uses (picchio.c:204-249), e.g. "layer0.pre_moe_norm".
  * Requires pc_set_trace(ctx, 1) before the step. */
@@ -239,14 +247,16 @@ pc_status pc_qt_matmul(pc_qt *w, const float *x_dev, float *y_dev, int S, void *
  * that forbids new allocations, or that cannot afford the implicit
  * synchronization cudaMalloc brings.  pc_qt_matmul allocates a job table the
  * first time it sees each row count S; this entry point allocates nothing, at
- * any call: its scratch (job table, job count, error word, ~1 KB) is a static
- * device array of this library, set up once per device on the first call
- * (cudaGetSymbolAddress plus a synchronous clear of the error word) - make
- * that first call before any stream capture that would include it.
+ * any call: its scratch (the GEMV job table and job count, ~1 KB) is a static
+ * device array of this library that every GPU loading the library holds
+ * until exit.  The first call on a device looks up that array's device
+ * address (cudaGetSymbolAddress) - make that first call before any stream
+ * capture that would include it.  Every call rewrites the whole table before
+ * the GEMV reads it.
  * Limits: S <= PC_QT_NOALLOC_MAX_ROWS (PC_ERR_RANGE beyond); one scratch per
  * device, so calls that overlap in time (other streams or threads) race and
- * must be serialized by the caller.  No counterpart in the reference, whose
- * matmul_qt (quant.h:323-337) runs on the host with caller-owned buffers. */
+ * must be serialized by the caller.  This entry point has no counterpart in
+ * the reference. */
 #define PC_QT_NOALLOC_MAX_ROWS 64
 pc_status pc_qt_matmul_noalloc(pc_qt *w, const float *x_dev, float *y_dev, int S, void *stream);
 /* out_dev[O][I] = dequantized weights, (nibble-8)*scale in fp32. */

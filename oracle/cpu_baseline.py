@@ -45,9 +45,15 @@ def _setup_ref():
 def measure(D=2880, H=64, KVH=8, hd=64, E=128, K=4, inter=2880, V=201088, gs=32, n_layers=36,
             ctx=4096, window=128, budget_s=20.0, threads=None) -> dict:
     """Returns {"tok_s", "layer_full_ms", "layer_sliding_ms", "head_ms", "cores", "kind", "sample"}."""
-    threads = threads or os.cpu_count() or 1
+    threads = threads or len(os.sched_getaffinity(0)) or 1
     os.environ["OMP_NUM_THREADS"] = str(threads)
     R = _setup_ref()
+    if R is not None and hasattr(R, "ref_set_threads"):
+        # the OpenMP runtime may already be up (torch loads it; torchrun sets
+        # OMP_NUM_THREADS=1): set the team size directly and read it back
+        R.ref_set_threads(threads)
+        R.ref_max_threads.restype = C.c_int
+        threads = int(R.ref_max_threads())
     rng = np.random.default_rng(0)
     I2 = 2 * inter
     f32 = np.float32
@@ -128,6 +134,44 @@ def measure(D=2880, H=64, KVH=8, hd=64, E=128, K=4, inter=2880, V=201088, gs=32,
                    f"timed and scaled to {n_full}+{n_slide} layers, plus INT8 lm_head on {vs} of {V} rows "
                    f"scaled to {V}; {'reference functions from oracle/_ref, OpenMP ' + str(threads) + ' threads' if R is not None else 'oracle port, 1 thread'}"),
     }
+
+
+def measure_e2e(threads=None, prompt_len=64, steps=32, seed=1234) -> dict | None:
+    """The unmodified reference binary (oracle/_ref/picchio) end to end on
+    BASELINE configs[0], the tiny seeded model: a prompt_len-id random prompt,
+    then `steps` greedy tokens (MODEL, INPUT_FILE, OUTPUT=ids, TEMPERATURE=0,
+    REP=1; ECAP = every expert, so the expert cache holds the whole model).
+    Returns the decode and prefill rates the binary itself reports, or None
+    when the binary has not been built."""
+    import re
+    import subprocess
+    import tempfile
+
+    from picchio_b200.synth import SynthConfig, make_model, random_prompt
+    if not os.path.exists(O.REF_BIN_PATH):
+        return None
+    threads = threads or len(os.sched_getaffinity(0)) or 1
+    cfg = SynthConfig()
+    with tempfile.TemporaryDirectory() as d:
+        make_model(d, cfg, seed)
+        pf = os.path.join(d, "prompt.txt")
+        with open(pf, "w") as f:
+            f.write(" ".join(map(str, random_prompt(prompt_len, cfg.vocab_size, 7))))
+        env = dict(os.environ, MODEL=d, INPUT_FILE=pf, OUTPUT="ids", TEMPERATURE="0", REP="1", MAX=str(steps),
+                   CTX="512", ECAP=str(cfg.num_local_experts), OMP_NUM_THREADS=str(threads))
+        r = subprocess.run([O.REF_BIN_PATH], env=env, capture_output=True, text=True, cwd=d, timeout=300)
+    if r.returncode != 0:
+        return None
+    gen = re.search(r"generated (\d+) tokens in ([0-9.]+) s", r.stderr)
+    pre = re.search(r"prefill in ([0-9.]+) s", r.stderr)
+    if not gen:
+        return None
+    n, t = int(gen.group(1)), float(gen.group(2))
+    return {"value": n / t if t > 0 else None, "unit": "tok/s", "cores": threads, "kind": "reference",
+            "prefill_s": float(pre.group(1)) if pre else None,
+            "sample": (f"unmodified reference binary end to end on the tiny seeded model (configs[0]): "
+                       f"{prompt_len}-id prompt, {n} greedy tokens, OMP_NUM_THREADS={threads}, "
+                       f"decode rate as the binary reports it")}
 
 
 if __name__ == "__main__":

@@ -33,10 +33,31 @@ _u8p = C.POINTER(C.c_uint8)
 _ip = C.POINTER(C.c_int)
 
 
+def reference_dir():
+    """The reference's source directory: the REF environment variable, else
+    the ``reference_path`` of the repository's BASELINE.json; None when
+    neither names an existing directory (e.g. on a GPU box, which only gets
+    the prebuilt oracle/_ref)."""
+    cand = os.environ.get("REF")
+    if not cand:
+        try:
+            with open(os.path.join(os.path.dirname(HERE), "BASELINE.json")) as f:
+                cand = json.load(f).get("reference_path")
+        except (OSError, ValueError):
+            cand = None
+    return cand if cand and os.path.isfile(os.path.join(cand, "picchio.c")) else None
+
+
 def build(ref: bool = False) -> None:
-    """Compile the oracle (and, with ref=True, the reference) via oracle/Makefile."""
-    targets = ["oracle"] + (["ref"] if ref else [])
-    subprocess.run(["make", "-s", "-C", HERE] + targets, check=True)
+    """Compile the oracle (and, with ref=True, the reference from
+    reference_dir()) via oracle/Makefile."""
+    args = ["make", "-s", "-C", HERE, "oracle"]
+    if ref:
+        src = reference_dir()
+        if src is None:
+            raise RuntimeError("reference sources not found: set REF to the reference checkout")
+        args += ["ref", f"REF={src}"]
+    subprocess.run(args, check=True)
 
 
 def _ptr(a: np.ndarray, t):

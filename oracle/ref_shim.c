@@ -138,3 +138,10 @@ REF_API int ref_sample_logits(float *logits, int vocab, float temperature, float
     *rng = g_rng;
     return id;
 }
+
+/* The OpenMP team size of the reference's parallel loops (#pragma omp
+ * parallel for in quant.h's matmuls): set before timing, whatever
+ * OMP_NUM_THREADS said when the runtime started, and read back. */
+#include <omp.h>
+REF_API void ref_set_threads(int n) { omp_set_num_threads(n); }
+REF_API int ref_max_threads(void) { return omp_get_max_threads(); }

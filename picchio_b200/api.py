@@ -133,6 +133,7 @@ def lib():
         L.pc_moe_layer.argtypes = [vp, C.c_int, vp, vp, C.c_int]
         L.pc_moe_experts.argtypes = [vp, C.c_int, vp, vp, vp, C.c_int, vp]
         L.pc_set_trace.argtypes = [vp, C.c_int]
+        L.pc_get_routing.argtypes = [vp, ip, C.c_int, ip]
         L.pc_get_stage.argtypes = [vp, C.c_char_p, fp, C.c_int]
         L.pc_dump.argtypes = [vp, C.c_char_p]
         L.pc_expert_prefetch.argtypes = [vp, C.c_int, ip, C.c_int]
@@ -169,6 +170,7 @@ def lib():
             getattr(L, name).restype = st
         for name in ("pc_init", "pc_init_synthetic", "pc_get_config", "pc_forward_token", "pc_prefill",
                      "pc_decode_batch", "pc_get_logits", "pc_moe_layer", "pc_moe_experts", "pc_set_trace",
+                     "pc_get_routing",
                      "pc_get_stage", "pc_dump", "pc_expert_prefetch", "pc_qt_create", "pc_qt_matmul", "pc_qt_matmul_noalloc",
                      "pc_qt_dequant", "pc_nccl_unique_id", "pc_check_device"):
             getattr(L, name).restype = st
@@ -369,6 +371,15 @@ class Model:
 
     def set_trace(self, on: bool = True):
         _check(lib().pc_set_trace(self._h, int(on)))
+
+    def routing(self) -> np.ndarray:
+        """Router top-k of the last step: int32 [n_layers, rows, topk] expert ids."""
+        L, K = self.config["n_layers"], self.config["topk"]
+        rows = C.c_int()
+        lib().pc_get_routing(self._h, None, 0, C.byref(rows))  # row count only
+        v = np.empty(max(L * rows.value * K, 1), np.int32)
+        _check(lib().pc_get_routing(self._h, v.ctypes.data_as(C.POINTER(C.c_int)), v.size, C.byref(rows)))
+        return v[:L * rows.value * K].reshape(L, rows.value, K)
 
     def stage(self, name: str, n: int) -> np.ndarray:
         v = np.empty(n, np.float32)

@@ -26,7 +26,7 @@ ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 COMMON = ["-O3", "-std=c++17", "-lineinfo", "-fmad=false", "-Xcompiler", "-fPIC,-ffp-contract=off,-O2",
           "-I" + INCLUDE, "-I" + CSRC]
 
-SOURCES = ["gemv.cu", "tcgemm.cu", "sample.cu", "decode.cu", "attention.cu", "attention_tc.cu", "kernels.cu", "weights.cu", "load.cu", "model.cu", "qt.cu", "host_io.cpp", "ep.cpp", "residency.cpp"]
+SOURCES = ["gemv.cu", "tcgemm.cu", "sample.cu", "attention.cu", "attention_tc.cu", "kernels.cu", "weights.cu", "load.cu", "model.cu", "qt.cu", "host_io.cpp", "ep.cpp", "residency.cpp"]
 
 
 def _newer(src_paths, out):

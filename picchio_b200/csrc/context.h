@@ -8,7 +8,6 @@
 #include <vector>
 
 #include "../../include/picchio_b200.h"
-#include "decode.h"
 #include "layout.h"
 #include "residency.h"
 #include "sample.h"
@@ -88,7 +87,9 @@ struct pc_ctx {
     float *h = nullptr, *hn = nullptr, *qbuf = nullptr, *attn = nullptr, *tmp = nullptr;
     float *act = nullptr, *eo = nullptr, *moe_out = nullptr, *logits = nullptr, *raw = nullptr;
     float *rlogits = nullptr, *rw = nullptr;
-    int *sel = nullptr, *pair_local = nullptr, *njobs = nullptr;
+    int *sel = nullptr;  // router selections of the last step, [layer][maxm][topk]
+    int route_rows = 0;  // rows of the last step's selections (pc_get_routing)
+    int *pair_local = nullptr, *njobs = nullptr;
     pc::GemvJob *jobs_gu = nullptr, *jobs_dn = nullptr;
     unsigned *router_ctr = nullptr, *attn_ctr = nullptr;
     float *attn_part = nullptr;
@@ -126,12 +127,6 @@ struct pc_ctx {
     // router's expert-sorted pair lists
     pc::TcExpState tex;
     int *pair_start = nullptr, *pair_list = nullptr;
-
-    // persistent decode kernel (decode.cu): 0 = not set up yet, 1 = used, -1 = not applicable
-    int dec_state = 0;
-    pc::DecodeArgs dec_args{};
-    size_t dec_smem = 0;
-    unsigned *gbar = nullptr;   // its grid barrier counter
 
     // on-device greedy loop (pc_generate)
     int *d_gen = nullptr;       // ids produced by the loop

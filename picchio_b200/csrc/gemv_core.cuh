@@ -528,9 +528,8 @@ constexpr int BAR_FILL = 1;  // named barrier 1: all threads (B refills); 2..15:
 // FMT: TF_T4 / TF_T8; NT: 1 or 2 N-tiles (<= 4 or <= 8 input rows); GS:
 // INT4 group size (0 = per row).
 // The GEMV work of one CTA (index cta of ncta) over the job list of p.  PDL:
-// the launch is a programmatic dependent launch (gemv_kernel); the persistent
-// decode kernel calls this with PDL = false between its own grid barriers,
-// and with smaller register steps (MBX blocks) to leave it registers.
+// the launch is a programmatic dependent launch (gemv_kernel); MBX > 0
+// overrides the blocks per ring step.
 template <int FMT, int NT, int GS, bool PDL, int MBX = 0>
 __device__ __forceinline__ void gemv_cta(const GemvParams &p, uint8_t *smem, int cta, int ncta) {
     constexpr int CPB = FMT == TF_T4 ? 2 : 1;  // 32-column MMA steps per block

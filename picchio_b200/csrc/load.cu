@@ -432,7 +432,7 @@ pc_status alloc_runtime(pc_ctx *c) {
     c->max_logit_rows = c->nseq;
     PC_TRY(dalloc(c, (size_t)c->max_logit_rows * k.vocab * 4, (void **)&c->logits));
     PC_TRY(dalloc(c, (size_t)M * k.n_experts * 4, (void **)&c->rlogits));
-    PC_TRY(dalloc(c, (size_t)M * K * 4, (void **)&c->sel));
+    PC_TRY(dalloc(c, (size_t)std::max(1, k.n_layers) * M * K * 4, (void **)&c->sel));  // [layer][row][k]
     PC_TRY(dalloc(c, (size_t)M * K * 4, (void **)&c->rw));
     PC_TRY(dalloc(c, (size_t)M * K * 4, (void **)&c->pair_local));
     PC_TRY(dalloc(c, 16, (void **)&c->njobs));

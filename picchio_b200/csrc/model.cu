@@ -18,7 +18,6 @@
 #include <vector>
 
 #include "context.h"
-#include "decode.h"
 #include "ep.h"
 #include "gemv.h"
 #include "host_io.h"
@@ -53,7 +52,6 @@ pc_status device_setup(int dev, int *nsm, int *max_smem) {
     std::lock_guard<std::mutex> lk(g_cfg_mu);
     if (dev >= 0 && dev < 64 && !g_configured[dev]) {
         PC_CU(gemv_configure(*max_smem));
-        PC_CU(decode_configure(*max_smem));
         PC_CU(tc_configure());
         PC_CU(kernels_configure());
         PC_CU(attention_tc_configure());
@@ -320,6 +318,9 @@ void trace_row_i(pc_ctx *c, const std::string &name, const int *dev, int n) {
     c->stages[name] = std::move(f);
 }
 
+// Layer l's slice of the router selections ([maxm][topk] expert ids).
+int *layer_sel(pc_ctx *c, int l) { return c->sel + (size_t)l * c->maxm * c->cfg.topk; }
+
 // The MoE block of one layer for M rows whose normalized states are x:
 // router (or given routing), gate_up + SwiGLU, down, combine.
 // With next_ln set, the combine also writes c->hn = rmsnorm(h, next_ln): the
@@ -376,7 +377,8 @@ pc_status run_moe_tc(pc_ctx *c, int l, const float *x, int M, float *out, float 
     }
     c->launches += 4;
     if (ep) PC_TRY(ep_allreduce_sum(c, c->eo, (size_t)P * D));
-    PC_CU(launch_combine(c->eo, c->rw, c->sel, k.routed_scale, M, K, D, out, h, c->st, next_ln, k.eps, c->hn));
+    PC_CU(launch_combine(c->eo, c->rw, layer_sel(c, l), k.routed_scale, M, K, D, out, h, c->st, next_ln, k.eps,
+                         c->hn));
     ++c->launches;
     return PC_OK;
 }
@@ -400,7 +402,8 @@ pc_status run_moe(pc_ctx *c, int l, const float *x, int M, const int *sel_in, co
     r.K = K;
     r.bias_first = bias_first;
     r.logits = c->rlogits;
-    r.sel = c->sel;
+    r.sel = layer_sel(c, l);
+    c->route_rows = M;
     r.w = c->rw;
     r.counter = c->router_ctr;
     r.sel_in = sel_in;
@@ -453,7 +456,7 @@ pc_status run_moe(pc_ctx *c, int l, const float *x, int M, const int *sel_in, co
     if (c->trace) {
         const int last = M - 1;
         trace_row(c, "layer" + std::to_string(l) + ".router_logits", c->rlogits + (size_t)last * k.n_experts, k.n_experts);
-        trace_row_i(c, "layer" + std::to_string(l) + ".top_indices", c->sel + (size_t)last * K, K);
+        trace_row_i(c, "layer" + std::to_string(l) + ".top_indices", layer_sel(c, l) + (size_t)last * K, K);
         trace_row(c, "layer" + std::to_string(l) + ".top_weights", c->rw + (size_t)last * K, K);
     }
     if (tc_exp) return run_moe_tc(c, l, x, M, out, h, next_ln);
@@ -495,7 +498,8 @@ pc_status run_moe(pc_ctx *c, int l, const float *x, int M, const int *sel_in, co
                       c->eo + ((size_t)last * K + kk) * D, D);
         }
     }
-    PC_CU(launch_combine(c->eo, c->rw, c->sel, k.routed_scale, M, K, D, out, h, c->st, next_ln, k.eps, c->hn));
+    PC_CU(launch_combine(c->eo, c->rw, layer_sel(c, l), k.routed_scale, M, K, D, out, h, c->st, next_ln, k.eps,
+                         c->hn));
     ++c->launches;
     return PC_OK;
 }
@@ -749,164 +753,9 @@ pc_status run_graph(pc_ctx *c, uint64_t key, F &&body) {
     return PC_OK;
 }
 
-// The persistent decode kernel (decode.cu) applies to batch-1 steps of models
-// whose dense weights are INT8 and experts INT4 with a supported group size
-// and head size, on one GPU, without tracing or per-kernel profiling.  It is
-// opt-in (PICCHIO_PERSISTENT=1): its stages are still slower than the
-// per-operation launches they replace.  Sets c->dec_state to 1 (use) or -1.
-pc_status decode_setup(pc_ctx *c) {
-    if (c->dec_state != 0) return PC_OK;
-    c->dec_state = -1;
-    if (c->res.on) return PC_OK;  // the persistent kernel indexes the HBM expert table
-    const char *env = getenv("PICCHIO_PERSISTENT");
-    if (!env || env[0] != '1') return PC_OK;
-    const pc_model_cfg &k = c->cfg;
-    const int D = k.hidden, H = k.n_heads, KVH = k.n_kv_heads, hd = k.head_dim, K = k.topk;
-    if (c->opts.ep_size > 1 || K > GEMV_INLINE_JOBS || k.n_experts > 256 || (D & 3) || D > 16 * GEMV_THREADS)
-        return PC_OK;
-    if (c->lm_head.t.fmt != TF_T8 || c->eg.gu.fmt != TF_T4 || c->eg.dn.fmt != TF_T4 || c->eg.gu.gs != c->eg.dn.gs)
-        return PC_OK;
-    if (!decode_supported(hd, c->eg.gu.gs) || c->e_lo != 0 || c->e_hi != k.n_experts) return PC_OK;
-    size_t need = std::max({gemv_smem_bytes(TF_T8, 1, c->lm_head.t.Ip, c->lm_head.t.blk_bytes),
-                            gemv_smem_bytes(TF_T4, 1, c->eg.gu.Ip, c->eg.gu.blk_bytes),
-                            gemv_smem_bytes(TF_T4, 1, c->eg.dn.Ip, c->eg.dn.blk_bytes)});
-    for (auto &ly : c->L) {
-        if (ly.wq.t.fmt != TF_T8 || ly.wk.t.fmt != TF_T8 || ly.wv.t.fmt != TF_T8 || ly.wo.t.fmt != TF_T8) return PC_OK;
-        need = std::max({need, gemv_smem_bytes(TF_T8, 1, ly.wq.t.Ip, ly.wq.t.blk_bytes),
-                         gemv_smem_bytes(TF_T8, 1, ly.wo.t.Ip, ly.wo.t.blk_bytes)});
-    }
-    const size_t smem = decode_smem_bytes(D, (int)need);
-    if (smem > (size_t)c->max_smem) return PC_OK;
-    DenseJobs *dj = nullptr;
-    PC_TRY(dense_jobs(c, 1, 0, &dj));
-    std::vector<DecodeLayer> layers(k.n_layers);
-    for (int l = 0; l < k.n_layers; ++l) {
-        Layer &ly = c->L[l];
-        DecodeLayer &d = layers[l];
-        memset(&d, 0, sizeof d);
-        GemvParams &q = d.qkv;
-        params_for(q, ly.wq.t, EPI_QKV);
-        use_jobs(q, dj, dj->qkv_off[l], dj->qkv_cnt_idx[l]);
-        q.shared_rows = 1;
-        q.ldx = D;
-        q.rope_cs = c->rope_cs;
-        q.rope_sn = c->rope_sn;
-        q.row_pos = c->d_pos;
-        q.row_seq = c->d_seq_rows;
-        q.qbuf = c->qbuf;
-        q.ldq = H * hd;
-        q.kcache = c->kc[l];
-        q.vcache = c->vc[l];
-        q.kv_bf16 = c->opts.kv_bf16;
-        q.kv_seq_stride = c->seq_stride;
-        q.kv_ctx = c->kv_ctx;
-        q.kv_dim = KVH * hd;
-        q.err = c->err;
-        GemvParams &o = d.o;
-        params_for(o, ly.wo.t, EPI_STORE);
-        use_jobs(o, dj, dj->o_off[l], dj->o_cnt_idx[l]);
-        o.shared_rows = 1;
-        o.x = c->attn;
-        o.ldx = H * hd;
-        o.y = c->h;         // hA
-        o.ldy = D;
-        o.residual = 1;
-        o.res_src = c->tmp;  // hB
-        o.err = c->err;
-        if (q.n_inline == 0 || o.n_inline == 0) return PC_OK;
-        AttnParams &a = d.attn;
-        a.q = c->qbuf; a.out = c->attn; a.kc = c->kc[l]; a.vc = c->vc[l]; a.kv_bf16 = c->opts.kv_bf16;
-        a.seq_stride = c->seq_stride; a.ctx = c->kv_ctx; a.sinks = ly.sinks; a.row_pos = c->d_pos;
-        a.row_seq = c->d_seq_rows; a.M = 1; a.H = H; a.KVH = KVH; a.hd = hd;
-        a.window = ly.layer_type == 0 ? k.sliding_window : 0;
-        a.part = c->attn_part; a.counter = c->attn_ctr; a.nsplit = 1;
-        d.in_ln = ly.in_ln;
-        d.post_ln = ly.post_ln;
-        d.router_w = ly.router;
-        d.router_b = ly.router_bias;
-        d.experts = ly.experts;
-    }
-    DecodeBlocks b;
-    memset(&b, 0, sizeof b);
-    params_for(b.gu, c->eg.gu, EPI_SWIGLU);
-    b.gu.ldx = D;
-    b.gu.y = c->act;
-    b.gu.ldy = k.intermediate;
-    b.gu.swiglu_limit = k.swiglu_limit;
-    b.gu.swiglu_alpha = k.swiglu_alpha;
-    b.gu.shared_rows = 1;
-    b.gu.err = c->err;
-    params_for(b.dn, c->eg.dn, EPI_STORE);
-    b.dn.x = c->act;
-    b.dn.ldx = k.intermediate;
-    b.dn.y = c->eo;
-    b.dn.ldy = D;
-    b.dn.shared_rows = 0;
-    b.dn.err = c->err;
-    params_for(b.lm, c->lm_head.t, EPI_LOGITS);
-    use_jobs(b.lm, dj, dj->lm_off, dj->lm_cnt_idx);
-    if (b.lm.n_inline != 1) return PC_OK;
-    b.lm.shared_rows = 1;
-    b.lm.ldx = D;
-    b.lm.y = c->logits;
-    b.lm.ldy = k.vocab;
-    b.lm.argmax = c->argmax;
-    b.lm.err = c->err;
-    DecodeLayer *d_layers = nullptr;
-    DecodeBlocks *d_blocks = nullptr;
-    PC_TRY(dalloc(c, layers.size() * sizeof(DecodeLayer), (void **)&d_layers));
-    PC_TRY(dalloc(c, sizeof(DecodeBlocks), (void **)&d_blocks));
-    PC_TRY(dalloc(c, 16, (void **)&c->gbar));
-    PC_CU(cudaMemcpy(d_layers, layers.data(), layers.size() * sizeof(DecodeLayer), cudaMemcpyHostToDevice));
-    PC_CU(cudaMemcpy(d_blocks, &b, sizeof b, cudaMemcpyHostToDevice));
-    DecodeArgs &a = c->dec_args;
-    memset(&a, 0, sizeof a);
-    a.layers = d_layers;
-    a.blocks = d_blocks;
-    a.L = k.n_layers; a.D = D; a.E = k.n_experts; a.K = K; a.V = k.vocab;
-    a.eps = k.eps; a.routed_scale = k.routed_scale;
-    a.emb_fmt = c->emb_fmt; a.emb_gs = c->emb_gs; a.emb = c->emb; a.emb_s = c->emb_s;
-    a.final_norm = c->final_norm;
-    a.ex_stride = c->eg.stride; a.ex_off_gu = c->eg.off_gu; a.ex_off_dn = c->eg.off_dn;
-    a.ex_off_gu_rs = c->eg.off_gu_rs; a.ex_off_dn_rs = c->eg.off_dn_rs;
-    a.ex_off_gu_b = c->eg.off_gu_b; a.ex_off_dn_b = c->eg.off_dn_b;
-    a.gu_rt = c->eg.gu.Op / 16; a.dn_rt = c->eg.dn.Op / 16; a.gu_O = c->eg.gu.O; a.dn_O = c->eg.dn.O;
-    a.hA = c->h; a.hB = c->tmp; a.eo = c->eo; a.rlogits = c->rlogits; a.argmax = c->argmax;
-    a.d_tok = c->d_tok; a.d_pos = c->d_pos; a.d_next = c->d_next; a.d_gen = nullptr;
-    a.gbar = c->gbar; a.err = c->err;
-    c->dec_smem = smem;
-    c->dec_state = 1;
-    return PC_OK;
-}
-
-// nsteps greedy tokens from the token and position in d_tok / d_pos through
-// the persistent kernel (ids to d_next, and to gen when not null).
-pc_status decode_persistent(pc_ctx *c, int nsteps, int *gen) {
-    DecodeArgs a = c->dec_args;
-    a.d_gen = gen;
-    PC_CU(cudaMemsetAsync(c->gbar, 0, 16, c->st));
-    PC_CU(decode_launch(a, c->cfg.head_dim, c->opts.kv_bf16, c->eg.gu.gs, nsteps, c->nsm, c->dec_smem, c->st));
-    ++c->launches;
-    return PC_OK;
-}
-
 // Decode-shaped step (tokens/positions in h_tok/h_pos, M rows, KV slot =
 // row for batches, 0 for a single sequence): graph replay when enabled.
 pc_status decode_step(pc_ctx *c, int M, int *next) {
-    if (M == 1 && !c->trace && !c->prof && !c->smp.on) {
-        PC_TRY(decode_setup(c));
-        if (c->dec_state == 1) {
-            PC_CU(cudaMemcpyAsync(c->d_tok, c->h_tok, 4, cudaMemcpyHostToDevice, c->st));
-            PC_CU(cudaMemcpyAsync(c->d_pos, c->h_pos, 4, cudaMemcpyHostToDevice, c->st));
-            PC_TRY(decode_persistent(c, 1, nullptr));
-            PC_CU(cudaMemcpyAsync(c->h_next, c->d_next, 4, cudaMemcpyDeviceToHost, c->st));
-            PC_CU(cudaMemcpyAsync(c->h_err, c->err, 4, cudaMemcpyDeviceToHost, c->st));
-            PC_CU(cudaStreamSynchronize(c->st));
-            PC_TRY(check_err(c));
-            next[0] = c->h_next[0];
-            return PC_OK;
-        }
-    }
     int maxp = 0;
     for (int i = 0; i < M; ++i) maxp = std::max(maxp, c->h_pos[i]);
     const int ns = split_bucket(c, maxp);
@@ -937,8 +786,6 @@ pc_status generate(pc_ctx *c, int tok, int pos, int n, int *out, float *device_m
     DenseJobs *dj = nullptr;
     PC_TRY(dense_jobs(c, 1, 0, &dj));
     auto body = [&]() -> pc_status { return run_step(c, 1, c->d_seq_rows, 0, ns, dj, true); };
-    if (!c->trace && !c->prof) PC_TRY(decode_setup(c));
-    const bool persistent = c->dec_state == 1 && !c->trace && !c->prof && !c->smp.on;
     c->h_tok[0] = tok;
     c->h_pos[0] = pos;
     PC_CU(cudaMemcpyAsync(c->d_tok, c->h_tok, 4, cudaMemcpyHostToDevice, c->st));
@@ -948,11 +795,7 @@ pc_status generate(pc_ctx *c, int tok, int pos, int n, int *out, float *device_m
     PC_CU(cudaEventCreate(&e0));
     PC_CU(cudaEventCreate(&e1));
     PC_CU(cudaEventRecord(e0, c->st));
-    if (persistent) {
-        PC_TRY(decode_persistent(c, n, c->d_gen));
-    } else {
-        for (int i = 0; i < n; ++i) PC_TRY(run_graph(c, (1ull << 62) | (uint64_t)ns | sampler_key(c), body));
-    }
+    for (int i = 0; i < n; ++i) PC_TRY(run_graph(c, (1ull << 62) | (uint64_t)ns | sampler_key(c), body));
     PC_CU(cudaEventRecord(e1, c->st));
     PC_CU(cudaMemcpyAsync(out, c->d_gen, (size_t)n * 4, cudaMemcpyDeviceToHost, c->st));
     PC_CU(cudaMemcpyAsync(c->h_err, c->err, 4, cudaMemcpyDeviceToHost, c->st));
@@ -1358,6 +1201,18 @@ pc_status pc_moe_experts(pc_ctx *c, int layer, const float *x_dev, const int *se
     PC_CU(cudaStreamSynchronize(c->st));
     PC_TRY(check_err(c));
     return res_after_step(c);
+}
+
+pc_status pc_get_routing(pc_ctx *c, int *expert_ids, int cap, int *rows) {
+    PC_TRY(check_ctx(c));
+    if (!rows || cap < 0 || (cap > 0 && !expert_ids)) return fail(PC_ERR_INVALID_ARG, "bad pc_get_routing arguments");
+    const int L = c->cfg.n_layers, M = c->route_rows, K = c->cfg.topk;
+    *rows = M;
+    if ((int64_t)L * M * K > cap) return fail(PC_ERR_RANGE, "pc_get_routing needs n_layers * rows * topk ids");
+    PC_CU(cudaStreamSynchronize(c->st));
+    for (int l = 0; l < L && M > 0; ++l)
+        PC_CU(cudaMemcpy(expert_ids + (size_t)l * M * K, layer_sel(c, l), (size_t)M * K * 4, cudaMemcpyDeviceToHost));
+    return PC_OK;
 }
 
 pc_status pc_set_trace(pc_ctx *c, int on) {

@@ -66,12 +66,13 @@ pc_status jobs_for(pc_qt *w, int S, std::pair<GemvJob *, int *> &out) {
 // ---- pc_qt_matmul_noalloc: the same product, for callers that cannot allocate
 //
 // Scratch lives in one file-scope device array per device: the GEMV job
-// table (up to PC_QT_NOALLOC_MAX_ROWS input rows = 8 jobs of 8 rows), its job
-// count and the kernel's error word.  Its address is taken once per device
-// with cudaGetSymbolAddress, when the error word (the only field that must
-// start at zero) is also cleared; every call rewrites the job table with a
-// one-warp kernel and then launches the GEMV on it.  Nothing is allocated,
-// so two calls that overlap (different streams or threads) race on it.
+// table (up to PC_QT_NOALLOC_MAX_ROWS input rows = 8 jobs of 8 rows) and its
+// job count.  Its address is taken once per device with cudaGetSymbolAddress;
+// every call rewrites the job count and table with a one-warp kernel before
+// the GEMV reads them, so nothing in it has to start at zero.  Nothing is
+// allocated, so two calls that overlap (different streams or threads) race on
+// it.  The GEMV has no bounded waits and reports nothing through an error
+// word; launch failures come back from the launch itself.
 
 namespace {
 
@@ -80,7 +81,6 @@ constexpr int NOALLOC_MAX_JOBS = PC_QT_NOALLOC_MAX_ROWS / GEMV_MAXR;
 struct NoallocScratch {
     GemvJob jobs[NOALLOC_MAX_JOBS];
     int njobs;
-    int err;  // written by the GEMV on a fault; zero from set-up on
 };
 
 __device__ __align__(256) unsigned char g_noalloc_scratch[sizeof(NoallocScratch)];
@@ -89,7 +89,8 @@ constexpr int NOALLOC_MAX_DEVICES = 64;
 std::mutex g_noalloc_mu;
 NoallocScratch *g_noalloc_ptr[NOALLOC_MAX_DEVICES] = {};
 
-// Once per device (the current one): the scratch address and a zeroed error word.
+// Once per device (the current one): the device address of the scratch
+// array.  The host-side name g_noalloc_scratch is not a device address.
 pc_status noalloc_scratch(int dev, NoallocScratch **out) {
     if (dev < 0 || dev >= NOALLOC_MAX_DEVICES) return fail(PC_ERR_INVALID_ARG, "device ordinal out of range");
     std::lock_guard<std::mutex> lk(g_noalloc_mu);
@@ -97,8 +98,6 @@ pc_status noalloc_scratch(int dev, NoallocScratch **out) {
         void *p = nullptr;
         cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
         if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(noalloc scratch)");
-        e = cudaMemset(p, 0, sizeof(NoallocScratch));
-        if (e != cudaSuccess) return cuda_fail(e, "clearing noalloc scratch");
         g_noalloc_ptr[dev] = static_cast<NoallocScratch *>(p);
     }
     *out = g_noalloc_ptr[dev];
@@ -252,7 +251,7 @@ pc_status pc_qt_matmul_noalloc(pc_qt *w, const float *x_dev, float *y_dev, int S
     p.ldx = w->t.I;
     p.y = y_dev;
     p.ldy = w->t.O;
-    p.err = &s->err;
+    p.err = nullptr;
     const int nt = gemv_nt_for_rows(std::min(S, GEMV_MAXR));
     if (!gemv_plan(p, nt, w->max_smem)) return fail(PC_ERR_FORMAT, "input rows do not fit in shared memory");
     PC_CU(gemv_launch(p, nt, w->nsm, st));

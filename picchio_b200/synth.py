@@ -29,6 +29,7 @@ from __future__ import annotations
 import json
 import os
 import struct
+from concurrent.futures import ThreadPoolExecutor
 from dataclasses import dataclass, asdict, field
 
 import numpy as np
@@ -79,6 +80,13 @@ def quantize_int4(w: np.ndarray, group_size: int):
         sc = np.where(amax > 1e-8, amax / 7.0, 1e-8).astype(np.float32)
         q = np.clip(np.round(w / sc[:, None]), -8, 7).astype(np.int8)
         scales = sc
+    elif I % group_size == 0:
+        # whole groups: the loop below, one reshape at a time (same operations, same bits)
+        ng = I // group_size
+        blk = w.reshape(O, ng, group_size)
+        amax = np.max(np.abs(blk), axis=2)
+        scales = np.where(amax > 1e-8, amax / 7.0, 1e-8).astype(np.float32)
+        q = np.clip(np.round(blk / scales[:, :, None]), -8, 7).astype(np.int8).reshape(O, I)
     else:
         ng = (I + group_size - 1) // group_size
         scales = np.empty((O, ng), dtype=np.float32)
@@ -171,6 +179,7 @@ def make_model(out_dir: str, cfg: SynthConfig = TINY, seed: int = 1234) -> dict:
         else:
             raise ValueError(cfg.attn_format)
 
+    pool = ThreadPoolExecutor(max_workers=max(1, min(4, (os.cpu_count() or 1) - 1)))
     for l in range(L):
         p = f"model.layers.{l}."
         t[p + "input_layernorm.weight"] = (1.0 + normal((D,), 0.05)).astype(f32)
@@ -188,14 +197,29 @@ def make_model(out_dir: str, cfg: SynthConfig = TINY, seed: int = 1234) -> dict:
         t[p + "mlp.router.bias"] = normal((E,), 0.01)
         t[p + "mlp.experts.gate_up_proj_bias"] = normal((E, I2), 0.01)
         t[p + "mlp.experts.down_proj_bias"] = normal((E, D), 0.01)
-        for e in range(E):
-            pk, sc = quantize_int4(normal((I2, D), 0.02), cfg.group_size)
+        # draws stay in order on this thread; the quantization of each
+        # matrix runs on a worker while the next one is drawn
+        # (at most LAG experts in flight, which bounds the float copies held)
+        LAG = 4
+        futs = {}
+
+        def collect(e):
+            pk, sc = futs[e][0].result()
             t[p + f"mlp.experts.gate_up_proj.{e}"] = pk
             t[p + f"mlp.experts.gate_up_proj.{e}.qs"] = sc
-            pk, sc = quantize_int4(normal((D, Iin), 0.02), cfg.group_size)
+            pk, sc = futs.pop(e)[1].result()
             t[p + f"mlp.experts.down_proj.{e}"] = pk
             t[p + f"mlp.experts.down_proj.{e}.qs"] = sc
 
+        for e in range(E):
+            futs[e] = (pool.submit(quantize_int4, normal((I2, D), 0.02), cfg.group_size),
+                       pool.submit(quantize_int4, normal((D, Iin), 0.02), cfg.group_size))
+            if e >= LAG:
+                collect(e - LAG)
+        for e in range(max(0, E - LAG), E):
+            collect(e)
+
+    pool.shutdown()
     write_safetensors(os.path.join(out_dir, "model-00000.safetensors"), t)
     with open(os.path.join(out_dir, "config.json"), "w") as f:
         json.dump(cfg.config_json(), f, indent=1)

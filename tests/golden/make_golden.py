@@ -12,14 +12,17 @@ containers written by ``picchio_b200.synth`` and records:
 * ``kernels.npz``: reference ``matmul_qt`` outputs (quant.h:117-319) on seeded
   small inputs, via ``oracle/_ref/libpicchio_ref.so``.
 
-Needs ``/root/reference`` (or REF=...) only to build ``oracle/_ref``; the
+Needs the reference sources (``REF=...``, else BASELINE.json's
+``reference_path``) only to build ``oracle/_ref``; the
 fixtures it writes are small and committed, and the tests read only them.
-Usage: ``python tests/golden/make_golden.py``.
+Usage: ``python tests/golden/make_golden.py [tiny] [gptoss] [service]`` (all by default).
 """
 from __future__ import annotations
 
 import json
 import os
+import re
+import shutil
 import subprocess
 import sys
 import tempfile
@@ -132,9 +135,146 @@ def make_kernels():
     print("kernels.npz", len(out), "arrays")
 
 
+# GPT-OSS-shaped two-layer container: d_model 2880, 64 q / 8 kv heads x 64,
+# sinks, a 128-window layer and a full layer, 32 experts top-4 INT4 gs32,
+# INT8 dense weights; a 4096-id vocabulary keeps the file near 1 GB.  These
+# are the head and expert shapes of the GPT-OSS-20B/120B configurations.
+GPTOSS = dict(hidden_size=2880, num_hidden_layers=2, num_attention_heads=64, num_key_value_heads=8,
+              head_dim=64, intermediate_size=2880, num_local_experts=32, num_experts_per_tok=4,
+              vocab_size=4096, group_size=32, attn_format="i8")
+GPTOSS_SEED = 4321
+GPTOSS_PROMPT = 120      # decode then crosses positions 127/128/129 and 255/256/257
+GPTOSS_STEPS = 144       # forward_token calls after the prefill (positions 120..263)
+# calls whose stage tensors are kept (call s runs at position 120 + s - 1):
+# positions 126-130 (window edge of the sliding layer), 255-257, and the last
+GPTOSS_PROBES = [7, 8, 9, 10, 11, 136, 137, 138, 144]
+GPTOSS_PROBE_KEYS = ["layer0.output", "layer1.output", "layer0.attn_concat", "layer1.attn_concat",
+                     "final_norm"]
+GPTOSS_LONG_PROMPT = 300  # 1200 routed pairs: the expert GEMMs of a long prefill chunk
+GPTOSS_LONG_STEPS = 8
+
+
+# the stage tensors pc_get_stage exposes (the rest of the reference's dumps
+# are intermediate forms it has no separate buffer for)
+STAGE_RE = re.compile(r"^(embedding|final_norm|logits|layer\d+\.(input|pre_attn_norm|q_rope|attn_concat|attn_out|"
+                      r"post_attn_residual|pre_moe_norm|router_logits|top_indices|top_weights|"
+                      r"expert\d+\.(activated|output)|moe_out|output))$")
+
+
+def _dumps(d, pf, steps, threads):
+    dd = os.path.join(d, f"dumps{steps}")
+    os.makedirs(dd, exist_ok=True)
+    ids = run_ref(d, pf, steps, {"ORACLE_DIR": dd, "OMP_NUM_THREADS": str(threads)})
+    out = {fn[:-4]: np.load(os.path.join(dd, fn)) for fn in sorted(os.listdir(dd))}
+    return ids, out
+
+
+def make_gptoss(threads=8):
+    """gptoss_2l.json / gptoss_2l_dumps.npz: the reference's greedy ids for
+    GPTOSS_STEPS steps, the router top-k and logits of every one of those
+    forward_token calls (one reference run per call, each dumping its last
+    forward), the GPTOSS_PROBE_KEYS stage tensors at the probe calls, every
+    stage tensor of the last call, and the same for a GPTOSS_LONG_PROMPT-id
+    prompt over GPTOSS_LONG_STEPS calls."""
+    cfg = SynthConfig(**GPTOSS)
+    with tempfile.TemporaryDirectory() as d:
+        make_model(d, cfg, GPTOSS_SEED)
+        prompt = random_prompt(GPTOSS_PROMPT, cfg.vocab_size, 11)
+        pf = os.path.join(d, "prompt.txt")
+        with open(pf, "w") as f:
+            f.write(" ".join(map(str, prompt)))
+        thr = {"OMP_NUM_THREADS": str(threads)}
+        ids = run_ref(d, pf, GPTOSS_STEPS, thr)
+        arrays, topk, rlog = {}, [], []
+        for s in range(1, GPTOSS_STEPS + 1):
+            ids_s, dm = _dumps(d, pf, s, threads)
+            assert ids_s == ids[:s], s
+            topk.append([dm[f"layer{l}.top_indices"].reshape(-1).astype(int).tolist() for l in range(2)])
+            rlog.append(np.stack([dm[f"layer{l}.router_logits"].reshape(-1) for l in range(2)]))
+            if s in GPTOSS_PROBES:
+                for k in GPTOSS_PROBE_KEYS:
+                    arrays[f"probe{s}.{k}"] = dm[k].reshape(-1)
+            if s == GPTOSS_STEPS:
+                for k, v in dm.items():
+                    if STAGE_RE.match(k):
+                        arrays[f"last.{k}"] = v.reshape(-1)
+            shutil.rmtree(os.path.join(d, f"dumps{s}"))
+        arrays["router_logits"] = np.stack(rlog).astype(np.float32)
+        long_prompt = random_prompt(GPTOSS_LONG_PROMPT, cfg.vocab_size, 12)
+        pf2 = os.path.join(d, "prompt_long.txt")
+        with open(pf2, "w") as f:
+            f.write(" ".join(map(str, long_prompt)))
+        dd = os.path.join(d, "dumps_long")
+        os.makedirs(dd)
+        long_ids = run_ref(d, pf2, GPTOSS_LONG_STEPS, {"ORACLE_DIR": dd, **thr})
+        for fn in sorted(os.listdir(dd)):
+            if STAGE_RE.match(fn[:-4]):
+                arrays[f"long.{fn[:-4]}"] = np.load(os.path.join(dd, fn)).reshape(-1)
+    np.savez_compressed(os.path.join(HERE, "gptoss_2l_dumps.npz"), **arrays)
+    meta = dict(name="gptoss_2l", options=GPTOSS, seed=GPTOSS_SEED, prompt=prompt, steps=GPTOSS_STEPS, ctx=512,
+                ids=ids, top_indices=topk, probes=GPTOSS_PROBES, probe_keys=GPTOSS_PROBE_KEYS,
+                long_prompt=long_prompt, long_steps=GPTOSS_LONG_STEPS, long_ids=long_ids)
+    with open(os.path.join(HERE, "gptoss_2l.json"), "w") as f:
+        json.dump(meta, f)
+    print("gptoss_2l ids", ids[:12], "... long", long_ids)
+
+
+# The reference's command-line contract on the tiny model: a SERVICE=1
+# session (service_loop, picchio.c:2700-2795) with prefix reuse (TURN keep),
+# greedy and sampled turns, the range and vocabulary errors, RESET and
+# SHUTDOWN; and a one-shot OUTPUT=ids run from INPUT_FILE.  stdout is kept
+# byte for byte.
+SERVICE_ENV = {"CTX": "128", "SEED": "42", "REP": "1.1", "ECAP": "8"}
+
+
+def service_script(prompt):
+    p = prompt
+    turns = [
+        f"TURN 8 0 0 1 0 12 {' '.join(map(str, p[:12]))}",
+        f"TURN 6 20 0 1 0 5 {' '.join(map(str, p[12:17]))}",     # keep the whole first turn
+        f"TURN 5 7 0.8 0.9 40 4 {' '.join(map(str, p[17:21]))}",  # keep a prefix; sampled
+        f"TURN 4 999 0 1 0 3 {' '.join(map(str, p[21:24]))}",      # keep > pos: BAD_RANGE
+        "TURN 4 0 0 1 0 2 5 5000",                                  # id outside the vocabulary
+        "TURN 5 0 0 1 0 125 " + " ".join(map(str, (p * 3)[:125])),  # runs into the context end
+        "RESET",
+        f"TURN 6 0 1.0 0.95 50 10 {' '.join(map(str, p[24:34]))}",
+        "SHUTDOWN",
+    ]
+    return "\n".join(turns) + "\n"
+
+
+def make_service():
+    cfg = SynthConfig()
+    with tempfile.TemporaryDirectory() as d:
+        make_model(d, cfg, 1234)
+        prompt = random_prompt(PROMPT_LEN, cfg.vocab_size, 7)
+        script = service_script(prompt)
+        env = dict(os.environ, MODEL=d, SERVICE="1", OMP_NUM_THREADS="4", **SERVICE_ENV)
+        svc = subprocess.run([O.REF_BIN_PATH], env=env, input=script, capture_output=True, text=True, cwd=d,
+                             check=True).stdout
+        pf = os.path.join(d, "prompt.txt")
+        with open(pf, "w") as f:
+            f.write(" ".join(map(str, prompt)))
+        ids_env = {"OUTPUT": "ids", "TEMPERATURE": "0", "REP": "1", "MAX": "24", "CTX": "512"}
+        env = dict(os.environ, MODEL=d, INPUT_FILE=pf, OMP_NUM_THREADS="4", **ids_env)
+        ids_out = subprocess.run([O.REF_BIN_PATH], env=env, capture_output=True, text=True, cwd=d,
+                                 check=True).stdout
+    meta = dict(seed=1234, prompt=prompt, service_env=SERVICE_ENV, script=script, service_stdout=svc,
+                ids_env=ids_env, ids_stdout=ids_out)
+    with open(os.path.join(HERE, "service_tiny.json"), "w") as f:
+        json.dump(meta, f, indent=1)
+    print("service transcript:", svc.count("\n"), "lines;", "ids run:", ids_out.split()[:8])
+
+
 if __name__ == "__main__":
     O.build(ref=True)
-    for n, o in VARIANTS.items():
-        make_variant(n, o)
-    add_sampled("tiny_gs32_i8")
-    make_kernels()
+    which = sys.argv[1:] or ["tiny", "gptoss", "service"]
+    if "tiny" in which:
+        for n, o in VARIANTS.items():
+            make_variant(n, o)
+        add_sampled("tiny_gs32_i8")
+        make_kernels()
+    if "gptoss" in which:
+        make_gptoss()
+    if "service" in which:
+        make_service()

@@ -241,25 +241,6 @@ def test_bf16_kv_cache_stays_close(variant):
         assert rel_l2(b.logits(0), a.logits(0)) < 1e-2
 
 
-def test_persistent_decode_kernel_matches_reference(monkeypatch):
-    """The persistent batch-1 decode kernel (opt-in, PICCHIO_PERSISTENT=1)
-    gives the reference's greedy ids, per token (pc_forward_token) and in one
-    multi-token launch (pc_generate)."""
-    from picchio_b200 import Model
-    m = meta("tiny_gs32_i8")
-    import tempfile
-    d = tempfile.mkdtemp()
-    make_model(d, SynthConfig(**m["options"]), m["seed"])
-    monkeypatch.setenv("PICCHIO_PERSISTENT", "1")
-    with Model(d, ctx=m["ctx"]) as model:
-        ids = model.generate(m["prompt"], m["steps"])
-        assert ids == m["ids_batched"]
-        n = len(m["prompt"])
-        tok = model.prefill_tokens(m["prompt"], 0)
-        dev, _ = model.generate_device(tok, n, 32)
-        assert [tok] + dev[:31] == m["ids_batched"][:32]
-
-
 def test_tensor_core_split_k_prefill_matches_sequential():
     """A model wide enough that the tensor-core projections split K over
     several CTAs per 128-row tile (d_model 1024: 8 steps of 128 columns):
