@@ -22,12 +22,16 @@ full forward at positions 4096+.
   algorithmic bytes per launch = 4 experts x (gate_up tiles + gate_up bias).
 * cpu_baseline / --impl reference: the reference's own decode functions
   (oracle/_ref) on this host's cores, see oracle/cpu_baseline.py.
-* side measurements at N=1 (not the value): prefill (2048 ids in 1024-position
-  steps, expert and dense GEMMs on tcgen05), bs64 decode, and the
-  single-layer expert microbench of configs[1].
+* side measurements (not the value): bs64 decode at every N; at N=1 also
+  prefill (2048 ids in 1024-position steps, expert and dense GEMMs on
+  tcgen05), the single-layer expert microbench of configs[1], the
+  GPT-OSS-20B-shaped bs1 decode after a 512-id prompt and the
+  20B serving run, 16 x 2048-id prefill then batch-64 decode.
 
 Multi-GPU (torchrun): expert parallelism, experts split across ranks, the
-attention replicated; all ranks decode the same sequence (strong scaling).
+attention replicated; all ranks decode the same sequence (strong scaling);
+after each layer's down projection every rank writes its experts' output
+rows into the other GPUs' memory over NVLink (ep_push).
 """
 from __future__ import annotations
 
@@ -286,6 +290,72 @@ def prefill_bench(m, vocab, reps=2):
     return {"value": PREFILL_TOKENS / dt, "unit": "tok/s", "tokens": PREFILL_TOKENS, "chunk": PREFILL_CHUNK,
             "ms": dt * 1e3, "timing": "host clock around pc_prefill (ids H2D, next id D2H)",
             "kernel_ms": {k: v[0] for k, v in prof.items()}}
+
+
+def gptoss20b_bs1(dev, prompt_len=512, steps=256, warmup=3):
+    """a GPT-OSS-20B-shaped model (24 layers, 32 experts
+    top-4 INT4 gs32, seeded random weights) on one GPU, a prompt_len-id
+    seeded random prompt through pc_prefill (one prompt_len-position step:
+    dense and expert GEMMs on tcgen05), then `steps` greedy decode steps
+    (on-device loop, CUDA events), bf16 KV cache."""
+    import numpy as np
+    import torch
+    from picchio_b200 import Model, ModelConfig
+    cfg = ModelConfig.gpt_oss_20b()
+    ids = np.random.default_rng(20).integers(0, cfg.vocab, prompt_len).tolist()
+    with Model.synthetic(cfg, seed=2020, ctx=prompt_len + warmup + steps + 16, device=dev, kv_bf16=True,
+                         prefill_chunk=prompt_len) as m:
+        m.prefill_tokens(ids, 0)  # warm-up
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        tok = m.prefill_tokens(ids, 0)
+        t_pre = time.perf_counter() - t0
+        w, _ = m.generate_device(tok, prompt_len, warmup)
+        out, ms = m.generate_device(w[-1], prompt_len + warmup, steps)
+    return {"value": steps / (ms / 1e3), "unit": "tok/s", "batch": 1, "prompt": prompt_len, "steps": steps,
+            "ms_per_step": ms / steps, "prefill_tok_s": prompt_len / t_pre, "kv": "bf16",
+            "timing": "decode: CUDA events around the on-device greedy loop (pc_generate); prefill: host clock "
+                      "around pc_prefill"}
+
+
+def gptoss20b_serving(dev, nseq=16, prompt_len=2048, batch=64, steps=128, warmup=3):
+    """the GPT-OSS-20B-shaped model serving a batch:
+    nseq seeded random prompts of prompt_len ids, each through pc_prefill_seq
+    into its own KV slot (1024-position steps on tcgen05), then `steps`
+    batch-`batch` greedy decode steps (pc_decode_batch, host ints in and
+    out).  Slots nseq..batch-1 hold seeded prompt_len-position KV prefixes
+    (pc_kv_fill_synthetic): the decode reads the same bytes as for real
+    prompts.  Host clock around each phase."""
+    import numpy as np
+    import torch
+    from picchio_b200 import Model, ModelConfig
+    cfg = ModelConfig.gpt_oss_20b()
+    rng = np.random.default_rng(21)
+    prompts = [rng.integers(0, cfg.vocab, prompt_len).tolist() for _ in range(nseq)]
+    with Model.synthetic(cfg, seed=2021, ctx=prompt_len + warmup + steps + 16, device=dev, kv_bf16=True,
+                         max_batch=batch, prefill_chunk=PREFILL_CHUNK) as m:
+        m.prefill_tokens(prompts[0], 0, seq=0)  # warm-up
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        nxt = [m.prefill_tokens(p, 0, seq=s) for s, p in enumerate(prompts)]
+        t_pre = time.perf_counter() - t0
+        for s in range(nseq, batch):
+            m.kv_fill_synthetic(prompt_len, seq=s, seed=500 + s)
+        toks = nxt + [(7 * s + 1) % 1000 for s in range(nseq, batch)]
+        pos = [prompt_len] * batch
+        for _ in range(warmup):
+            toks = m.decode_batch(toks, pos)
+            pos = [q + 1 for q in pos]
+        t0 = time.perf_counter()
+        for _ in range(steps):
+            toks = m.decode_batch(toks, pos)
+            pos = [q + 1 for q in pos]
+        dt = time.perf_counter() - t0
+    return {"value": batch * steps / dt, "unit": "tok/s", "batch": batch, "steps": steps,
+            "ms_per_step": dt * 1e3 / steps, "prefill": {"value": nseq * prompt_len / t_pre, "unit": "tok/s",
+                                                         "sequences": nseq, "prompt": prompt_len,
+                                                         "chunk": PREFILL_CHUNK, "s": t_pre},
+            "kv": "bf16", "timing": "host clock around pc_prefill_seq / pc_decode_batch (host ids in and out)"}
 
 
 def moe_micro(dev, iters=20):
@@ -562,6 +632,8 @@ def main():
     m.close()
     if single_extra:
         line["moe_micro"] = moe_micro(local)
+        line["gptoss20b_bs1"] = gptoss20b_bs1(local)
+        line["gptoss20b_serving"] = gptoss20b_serving(local)
     if world > 1:
         # rank 0 replays the timed decode on one GPU (the same seeded model,
         # no expert parallelism) and compares the greedy ids

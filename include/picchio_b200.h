@@ -14,6 +14,13 @@
  *    promise are on the host.  A context is not thread-safe (nor is the
  *    reference: it keeps its state in globals).
  *  - Pointers named *_dev are device pointers; all others are host memory.
+ *    The context's stream does not wait for other streams: device inputs
+ *    must be complete when the call is made (synchronize the stream that
+ *    wrote them first).
+ *  - Expert parallelism (ep_size > 1): every rank makes the same calls in
+ *    the same order; each MoE block exchanges expert outputs between the
+ *    ranks' GPUs, and a rank that stops calling makes the others' next MoE
+ *    step fail with PC_ERR_TIMEOUT after about two seconds.
  *  - No torch types, no C++ types: plain pointers and sizes.
  */
 #ifndef PICCHIO_B200_H
@@ -53,7 +60,7 @@ typedef struct {
     int max_batch;     /* sequences served by pc_decode_batch (>= 1) */
     int ep_rank;       /* expert-parallel rank (0 when ep_size <= 1) */
     int ep_size;       /* expert-parallel group size; <= 1 means one GPU */
-    const void *nccl_id; /* 128-byte ncclUniqueId from rank 0 when ep_size > 1 */
+    const void *nccl_id; /* 128-byte ncclUniqueId from rank 0 when ep_size > 1 (one GPU per rank) */
     int use_graphs;    /* 1: replay decode steps as CUDA graphs */
     int expert_residency; /* 0: whole expert table in HBM; 1: pinned host + HBM cache */
     int expert_cache_slots; /* per layer, when expert_residency == 1 */
@@ -128,6 +135,13 @@ pc_status pc_forward_token(pc_ctx *ctx, int tok, int pos, int *next_tok);
  * The repetition history is seeded by the caller (pc_history_push), as
  * prefill_tokens seeds g_history before its blocks (picchio.c:1963-1967). */
 pc_status pc_prefill(pc_ctx *ctx, const int *ids, int n, int pos_base, int *next_tok);
+
+/* The same into KV slot `seq` of a batched-decode context (seq <
+ * opts.max_batch), so that pc_decode_batch row `seq` continues that prompt.
+ * The reference serves one sequence; this is prefill_tokens
+ * (picchio.c:1936-1975) per slot.  Greedy only (device sampling follows
+ * sequence 0). */
+pc_status pc_prefill_seq(pc_ctx *ctx, int seq, const int *ids, int n, int pos_base, int *next_tok);
 
 /* B independent sequences, one token each (sequence b uses KV slot b): the
  * batched-decode form of forward_token.  B <= opts.max_batch. */

@@ -394,16 +394,28 @@ def _load_qt(t: dict, name: str, O: int, I: int) -> QT:
     raise ValueError(f"{name}: dtype {dt} not handled by the oracle")
 
 
+def bf16_round(a):
+    """fp32 -> bf16 -> fp32 with round-to-nearest-even (what the device's
+    __float2bfloat16_rn stores), for finite values."""
+    u = np.ascontiguousarray(a, np.float32).view(np.uint32).astype(np.uint64)
+    u = (u + 0x7FFF + ((u >> 16) & 1)) & 0xFFFF0000
+    return u.astype(np.uint32).view(np.float32)
+
+
 class OracleModel:
     """forward_token (picchio.c:1655-1756) restated over oracle.c.
 
     The KV cache is fp32, as the reference keeps it (picchio.c:142-151).
+    With kv_bf16 every stored K and V row is rounded to bf16 first: the
+    device's bf16 cache, the one departure from the reference's arithmetic,
+    restated so that the device's bf16 path has an oracle of its own.
     ``forward_token`` returns the greedy next id; ``self.dumps`` holds the
     stage tensors of the last call under the reference's ORACLE_DIR names
     (picchio.c:204-249).
     """
 
-    def __init__(self, model_dir: str, ctx: int = 512):
+    def __init__(self, model_dir: str, ctx: int = 512, kv_bf16: bool = False):
+        self.kv_bf16 = kv_bf16
         self.c = c = cfg_load(model_dir)
         t = {}
         for fn in sorted(os.listdir(model_dir)):
@@ -486,8 +498,8 @@ class OracleModel:
             k[h * hd:(h + 1) * hd] = seg
         d[f"layer{l}.q_rope"], d[f"layer{l}.k_rope"] = q.copy(), k.copy()
         if pos < self.max_pos:
-            self.K[l][pos] = k
-            self.V[l][pos] = v
+            self.K[l][pos] = bf16_round(k) if self.kv_bf16 else k
+            self.V[l][pos] = bf16_round(v) if self.kv_bf16 else v
         end = min(pos, self.max_pos - 1)
         start = 0
         if ly["layer_type"] == 0:

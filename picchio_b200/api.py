@@ -128,6 +128,7 @@ def lib():
         L.pc_get_config.argtypes = [vp, C.POINTER(_Cfg)]
         L.pc_forward_token.argtypes = [vp, C.c_int, C.c_int, ip]
         L.pc_prefill.argtypes = [vp, ip, C.c_int, C.c_int, ip]
+        L.pc_prefill_seq.argtypes = [vp, C.c_int, ip, C.c_int, C.c_int, ip]
         L.pc_decode_batch.argtypes = [vp, ip, ip, C.c_int, ip]
         L.pc_get_logits.argtypes = [vp, C.c_int, fp, C.c_int]
         L.pc_moe_layer.argtypes = [vp, C.c_int, vp, vp, C.c_int]
@@ -168,7 +169,7 @@ def lib():
                      "pc_set_rng", "pc_get_rng", "pc_history_reset", "pc_history_push", "pc_history_get",
                      "pc_sample"):
             getattr(L, name).restype = st
-        for name in ("pc_init", "pc_init_synthetic", "pc_get_config", "pc_forward_token", "pc_prefill",
+        for name in ("pc_init", "pc_init_synthetic", "pc_get_config", "pc_forward_token", "pc_prefill", "pc_prefill_seq",
                      "pc_decode_batch", "pc_get_logits", "pc_moe_layer", "pc_moe_experts", "pc_set_trace",
                      "pc_get_routing",
                      "pc_get_stage", "pc_dump", "pc_expert_prefetch", "pc_qt_create", "pc_qt_matmul", "pc_qt_matmul_noalloc",
@@ -194,6 +195,16 @@ def _dev_ptr(t):
     if not t.is_cuda or not t.is_contiguous():
         raise ValueError("expected a contiguous CUDA tensor")
     return C.c_void_p(t.data_ptr())
+
+
+def _torch_done(*ts):
+    """Waits for torch's pending work on the tensors' devices: a context runs
+    on its own non-blocking stream, which is not ordered after torch's, so a
+    tensor torch is still writing (a host copy in flight) must be complete
+    before the library reads it."""
+    import torch
+    for dev in {t.device for t in ts}:
+        torch.cuda.current_stream(dev).synchronize()
 
 
 class Model:
@@ -252,10 +263,13 @@ class Model:
         _check(lib().pc_forward_token(self._h, int(tok), int(pos), C.byref(out)))
         return out.value
 
-    def prefill_tokens(self, ids, pos_base: int = 0) -> int:
+    def prefill_tokens(self, ids, pos_base: int = 0, seq: int = 0) -> int:
         a = (C.c_int * len(ids))(*[int(v) for v in ids])
         out = C.c_int()
-        _check(lib().pc_prefill(self._h, a, len(ids), int(pos_base), C.byref(out)))
+        if seq == 0:
+            _check(lib().pc_prefill(self._h, a, len(ids), int(pos_base), C.byref(out)))
+        else:
+            _check(lib().pc_prefill_seq(self._h, int(seq), a, len(ids), int(pos_base), C.byref(out)))
         return out.value
 
     def decode_batch(self, toks, pos) -> list:
@@ -294,7 +308,8 @@ class Model:
         """Ends profiling; returns {label: (total_ms, launches)}."""
         _check(lib().pc_profile_end(self._h))
         res = {}
-        for lab in ("expert_gate_up", "expert_down", "qkv", "o_proj", "lm_head", "attention", "router"):
+        for lab in ("expert_gate_up", "expert_down", "qkv", "o_proj", "lm_head", "attention", "router",
+                    "ep_exchange", "combine"):
             t, n = C.c_double(), C.c_int()
             _check(lib().pc_profile_get(self._h, lab.encode(), C.byref(t), C.byref(n)))
             if n.value:
@@ -341,6 +356,7 @@ class Model:
     def sample(self, logits) -> int:
         """One device draw from a [vocab] float32 CUDA tensor."""
         out = C.c_int(0)
+        _torch_done(logits)
         _check(lib().pc_sample(self._h, _dev_ptr(logits), C.byref(out)))
         return int(out.value)
 
@@ -358,6 +374,7 @@ class Model:
         """moe_forward for the rows of x ([M, D] float32 CUDA tensor)."""
         import torch
         out = torch.empty_like(x)
+        _torch_done(x, out)
         _check(lib().pc_moe_layer(self._h, layer, _dev_ptr(x), _dev_ptr(out), x.shape[0]))
         return out
 
@@ -365,6 +382,7 @@ class Model:
         """The expert half of moe_forward with routing given (sel int32 [M, K], w float32 [M, K])."""
         import torch
         out = torch.empty_like(x)
+        _torch_done(x, sel, w, out)
         _check(lib().pc_moe_experts(self._h, layer, _dev_ptr(x), _dev_ptr(sel), _dev_ptr(w), x.shape[0],
                                     _dev_ptr(out)))
         return out

@@ -8,6 +8,7 @@
 #include <vector>
 
 #include "../../include/picchio_b200.h"
+#include "kernels.h"
 #include "layout.h"
 #include "residency.h"
 #include "sample.h"
@@ -106,8 +107,15 @@ struct pc_ctx {
     // pinned host staging for one step's inputs / outputs
     int *h_tok = nullptr, *h_pos = nullptr, *h_next = nullptr;
 
-    // expert parallelism
+    // expert parallelism (ep.cpp): the NCCL communicator (set-up only) and
+    // the combine exchange over peer memory.  ep_blk[q] is rank q's exchange
+    // block (flags, then two receive buffers of maxm * topk * hidden floats),
+    // mapped into this process; ep_blk[ep_rank] is this rank's own.
     void *nccl_comm = nullptr;
+    int ep_n = 1, ep_rank = 0;
+    char *ep_blk[pc::EP_MAX_RANKS] = {};
+    int64_t ep_rx_bytes = 0;
+    unsigned *ep_state = nullptr;  // [0] epoch (exchanges completed), [1] push ticket
 
     bool trace = false;
     std::map<std::string, std::vector<float>> stages;
@@ -115,6 +123,7 @@ struct pc_ctx {
 
     int *d_seq_rows = nullptr;  // 0, 1, ..., maxm-1 (batched decode: row b -> sequence b)
     int *d_seq_zero = nullptr;  // all 0 (prefill: every row in sequence 0)
+    int *d_seq_one = nullptr;   // all one slot (pc_prefill_seq into a slot other than 0)
     int *h_err = nullptr;       // pinned mirror of the device error word
     std::vector<void *> allocs; // device allocations owned by the context
     void *pinned = nullptr;     // pinned staging block

@@ -59,9 +59,40 @@ static_assert(sizeof(SMeta) <= 640, "meta region");
 
 __host__ __device__ inline int off_B(int nt) { return (OFF_RED + NRED * nt * NCONS * 256 + 127) & ~127; }
 __host__ __device__ inline int off_ring(int nt, int Ip) { return (off_B(nt) + nt * Ip * 8 + 127) & ~127; }
-// Shared memory of one CTA: fixed regions, the B operand, the warps' rings.
-__host__ __device__ inline int gemv_smem_need(int fmt, int nt, int Ip, int blk_bytes) {
+// The warps' ring-slot mbarriers follow the rings (8-byte aligned: a ring
+// slot is a multiple of 64 bytes).
+__host__ __device__ inline int off_mbar(int fmt, int nt, int Ip, int blk_bytes) {
     return off_ring(nt, Ip) + NCONS * gemv_ring_depth(fmt, nt) * gemv_step_blocks(fmt, nt) * blk_bytes;
+}
+// Shared memory of one CTA: fixed regions, the B operand, the warps' rings
+// and their mbarriers.
+__host__ __device__ inline int gemv_smem_need(int fmt, int nt, int Ip, int blk_bytes) {
+    return off_mbar(fmt, nt, Ip, blk_bytes) + NCONS * gemv_ring_depth(fmt, nt) * 8;
+}
+// Bound on one wait for a ring slot's bulk copy (far above any real copy).
+constexpr unsigned long long GEMV_WAIT_NS = 1000000000ull;
+constexpr int GEMV_ERR_WAIT = 4;  // error word value when that wait gives up
+
+__device__ __forceinline__ unsigned long long gemv_now() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+// 1-D bulk copy global -> shared completing on bar (transaction bytes); no
+// multicast.  Both addresses 16-byte aligned, bytes a multiple of 16.
+__device__ __forceinline__ void gemv_bulk_load(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     smem_u32(dst)),
+                 "l"(src), "r"(bytes), "r"(smem_u32(bar))
+                 : "memory");
+}
+// Bounded wait for phase `parity` of bar; false when the bound ran out.
+__device__ __forceinline__ bool gemv_mbar_wait(uint64_t *bar, uint32_t parity) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const unsigned long long t0 = gemv_now();
+    while (!mbar_try_wait(bar, parity))
+        if (gemv_now() - t0 > GEMV_WAIT_NS) return false;
+    return true;
 }
 
 // Signed digits of v (|v| <= 2^22): v = hi * 2^16 + mid * 2^8 + lo with
@@ -562,15 +593,28 @@ __device__ __forceinline__ void gemv_cta(const GemvParams &p, uint8_t *smem, int
             meta->njobs = p.n_inline;
         }
     } else if (cw == 0) {  // prefix sum of row tiles over the device job table
-        if (PDL && !p.static_jobs) pdl_wait();  // the job table comes from the previous kernel
-        int nj = *p.njobs;
+        // A table written by the previous kernel needs the dependency wait.
+        // One written two or more kernels back (jobs_early) is complete once
+        // this grid runs: the kernel in between triggered this launch only
+        // after its own wait, which returned when the writer had finished.
+        // It is read through L2 (no line an older kernel left in L1).
+        const bool early = p.jobs_early != 0;
+        if (PDL && !p.static_jobs && !early) pdl_wait();
+        int nj = early ? __ldcg(p.njobs) : *p.njobs;
         nj = nj < 0 ? 0 : (nj > GEMV_MAX_JOBS ? GEMV_MAX_JOBS : nj);
         int run = 0;
         for (int base = 0; base < nj; base += 32) {
             int v = 0;
             if (base + lane < nj) {
-                v = p.jobs[base + lane].n_rt;
-                stiles[base + lane] = p.jobs[base + lane].tiles;
+                const GemvJob *jb = p.jobs + base + lane;
+                if (early) {
+                    v = __ldcg(&jb->n_rt);
+                    stiles[base + lane] = reinterpret_cast<const uint8_t *>(
+                        __ldcg(reinterpret_cast<const unsigned long long *>(&jb->tiles)));
+                } else {
+                    v = jb->n_rt;
+                    stiles[base + lane] = jb->tiles;
+                }
             }
 #pragma unroll
             for (int o = 1; o < 32; o <<= 1) {
@@ -640,25 +684,44 @@ __device__ __forceinline__ void gemv_cta(const GemvParams &p, uint8_t *smem, int
     // delays the latency-critical loads after the dependency wait: the input
     // row, the epilogue operands), the lm_head by 40 %.
     //
-    // This warp's ring of R step slots in shared memory, filled with
-    // cp.async (16 bytes per lane per copy, no registers held while in flight):
-    // step s lives in slot s % R; R - 1 steps are in flight behind the one
-    // being computed.
+    // This warp's ring of R step slots in shared memory: a step's blocks are
+    // contiguous in global memory, so lane 0 fetches each step with one bulk
+    // copy (the TMA engine, not the load/store pipeline) completing on the
+    // slot's mbarrier; step s lives in slot s % R; R - 1 steps are in flight
+    // behind the one being computed.  Tiles that may sit in mapped host
+    // memory (streamed residency) are copied by the lanes with cp.async
+    // instead, each lane's copies arriving on the same mbarrier.
     uint8_t *myring = smem + off_ring(NT, p.Ip) + (size_t)cw * R * MB * BB;
+    uint64_t *mybar = reinterpret_cast<uint64_t *>(smem + off_ring(NT, p.Ip) + (size_t)NCONS * R * MB * BB) + cw * R;
+    const bool lanes_copy = p.host_tiles != 0;
+    if (lane < R) mbar_init(mybar + lane, lanes_copy ? 32 : 1);
+    fence_mbar_init();
+    __syncwarp();
     const int sbytes = BB - 512;  // group-scale bytes per block (T4 with groups)
     int ld_u, ld_j, ld_c = 0, ld_seq = 0;
     first_from(j0, ld_u, ld_j);
     auto issue_step = [&]() {  // copies step (ld_u, ld_c), then moves the cursor on
         if (ld_u < u1) {
             const int nb = step_blocks(ld_c);
-            const uint8_t *src = slice(ld_u, ld_j) + (size_t)ld_c * MB * BB;
+            uint64_t *bar = mybar + ld_seq % R;
             uint8_t *dst = myring + (size_t)(ld_seq % R) * MB * BB;
+            const uint8_t *src = slice(ld_u, ld_j) + (size_t)ld_c * MB * BB;
+            if (lanes_copy) {
 #pragma unroll
-            for (int i = 0; i < MB; ++i) {
-                if (i < nb) {
-                    cp_async16(dst + i * BB + lane * 16, src + (size_t)i * BB + lane * 16);
-                    if (lane * 16 < sbytes)
-                        cp_async16(dst + i * BB + 512 + lane * 16, src + (size_t)i * BB + 512 + lane * 16);
+                for (int i = 0; i < MB; ++i) {
+                    if (i < nb) {
+                        cp_async16(dst + i * BB + lane * 16, src + (size_t)i * BB + lane * 16);
+                        if (lane * 16 < sbytes)
+                            cp_async16(dst + i * BB + 512 + lane * 16, src + (size_t)i * BB + 512 + lane * 16);
+                    }
+                }
+                cp_async_mbar_arrive(bar);
+            } else if (lane == 0) {
+                if (nb > 0) {
+                    mbar_arrive_expect_tx(bar, (uint32_t)(nb * BB));
+                    gemv_bulk_load(dst, src, (uint32_t)(nb * BB), bar);
+                } else {
+                    mbar_arrive(bar);  // an empty step (this warp's K share ended): completes at once
                 }
             }
             if (++ld_c == nch) {
@@ -666,7 +729,6 @@ __device__ __forceinline__ void gemv_cta(const GemvParams &p, uint8_t *smem, int
                 advance(ld_u, ld_j);
             }
         }
-        cp_async_commit();
         ++ld_seq;
     };
     // weights do not depend on earlier kernels: start streaming before waiting for them
@@ -701,8 +763,8 @@ __device__ __forceinline__ void gemv_cta(const GemvParams &p, uint8_t *smem, int
     int seq = 0;
     auto do_step = [&](int c) {
         issue_step();
-        cp_async_wait<R - 1>();
-        __syncwarp();  // every lane's copies of this step have landed
+        if (!gemv_mbar_wait(mybar + seq % R, (uint32_t)(seq / R) & 1u) && lane == 0 && p.err)
+            atomicExch(p.err, GEMV_ERR_WAIT);
         const uint8_t *slot = myring + (size_t)(seq % R) * MB * BB;
         ++seq;
         const int nb = step_blocks(c);

@@ -598,6 +598,73 @@ __global__ void __launch_bounds__(256) router_rows_kernel(const RouterParams r) 
     router_jobs(r, ssel, P, cnt, jstart, pstart, sorted);
 }
 
+// ---------------------------------------------------- expert-parallel ----
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned *p) {
+    unsigned v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void st_release_sys(unsigned *p, unsigned v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long ns_now() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+// Waits (bounded by EP_WAIT_NS) until every rank's flag reached exchange e;
+// false when the bound ran out.
+__device__ bool ep_wait_all(const unsigned *flags, int n, unsigned e) {
+    const unsigned long long t0 = ns_now();
+    for (int q = 0; q < n; ++q) {
+        while ((int)(ld_acquire_sys(flags + q) - e) < 0) {
+            if (ns_now() - t0 > (unsigned long long)EP_WAIT_NS) return false;
+            __nanosleep(64);
+        }
+    }
+    return true;
+}
+
+// Copies the output rows of this rank's (token, k) pairs into receive buffer
+// (e & 1) of every rank (itself included), e = this rank's exchange number
+// + 1; the last block to finish then publishes e in every rank's flag array.
+__global__ void __launch_bounds__(256) ep_push_kernel(const EpPushParams p) {
+    pdl_wait();
+    pdl_trigger();
+    const unsigned e = *reinterpret_cast<const volatile unsigned *>(p.state) + 1u;
+    const int64_t rx_off = EP_FLAG_BYTES + (int64_t)(e & 1u) * p.rx_bytes;
+    const bool v4 = (p.D & 3) == 0;
+    for (int pr = blockIdx.x; pr < p.P; pr += gridDim.x) {
+        if (!p.pair_local[pr]) continue;
+        if (v4) {
+            const int n4 = p.D >> 2;
+            const float4 *src = reinterpret_cast<const float4 *>(p.eo + (int64_t)pr * p.D);
+            for (int i = threadIdx.x; i < n4; i += blockDim.x) {
+                const float4 v = __ldcg(src + i);
+                for (int q = 0; q < p.n; ++q)
+                    reinterpret_cast<float4 *>(p.blk[q] + rx_off)[(int64_t)pr * n4 + i] = v;
+            }
+        } else {
+            for (int i = threadIdx.x; i < p.D; i += blockDim.x) {
+                const float v = __ldcg(p.eo + (int64_t)pr * p.D + i);
+                for (int q = 0; q < p.n; ++q) reinterpret_cast<float *>(p.blk[q] + rx_off)[(int64_t)pr * p.D + i] = v;
+            }
+        }
+    }
+    __threadfence_system();  // this thread's rows are visible to every rank
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        const unsigned t = atomicAdd(p.state + 1, 1u);
+        if (t == gridDim.x - 1) {  // last block: every row of this rank has been written
+            p.state[1] = 0u;
+            p.state[0] = e;
+            __threadfence_system();
+            for (int q = 0; q < p.n; ++q) st_release_sys(reinterpret_cast<unsigned *>(p.blk[q]) + p.rank, e);
+        }
+    }
+}
+
 // -------------------------------------------------------------- combine ----
 // One block per row; expert rows are taken four at a time with all their
 // loads in flight.  The fma chain runs in k order, as picchio.c:1445-1454
@@ -607,10 +674,18 @@ __global__ void __launch_bounds__(256) router_rows_kernel(const RouterParams r) 
 // (picchio.c:1712), computed exactly as rmsnorm_kernel computes it.
 __global__ void __launch_bounds__(NORM_THREADS) combine_kernel(const float *eo, const float *w, const int *sel,
                                                                 float scale, int K, int D, float *out, float *h,
-                                                                const float *ln_w, float eps, float *hn) {
+                                                                const float *ln_w, float eps, float *hn,
+                                                                const EpWait ep) {
     pdl_wait();
     pdl_trigger();
     const int m = blockIdx.x, tid = threadIdx.x;
+    if (ep.n > 0) {  // expert parallelism: the rows of every rank's pairs, once all have pushed
+        const unsigned e = *reinterpret_cast<const volatile unsigned *>(ep.state);
+        if (tid == 0 && !ep_wait_all(reinterpret_cast<const unsigned *>(ep.blk), ep.n, e))
+            atomicExch(ep.err, EP_ERR_WAIT);
+        __syncthreads();
+        eo = reinterpret_cast<const float *>(ep.blk + EP_FLAG_BYTES + (int64_t)(e & 1u) * ep.rx_bytes);
+    }
     const bool norm = ln_w && h;
     float wk[16];
     bool ok[16];
@@ -639,7 +714,7 @@ __global__ void __launch_bounds__(NORM_THREADS) combine_kernel(const float *eo, 
                 for (int j = 0; j < 3; ++j) {
                     const int i = tid + j * NORM_THREADS;
                     e[kk][j] = (k0 + kk < K && i < n4)
-                                   ? reinterpret_cast<const float4 *>(eo + ((int64_t)m * K + k0 + kk) * D)[i]
+                                   ? __ldcg(reinterpret_cast<const float4 *>(eo + ((int64_t)m * K + k0 + kk) * D) + i)
                                    : make_float4(0.f, 0.f, 0.f, 0.f);
                 }
 #pragma unroll
@@ -690,7 +765,7 @@ __global__ void __launch_bounds__(NORM_THREADS) combine_kernel(const float *eo, 
     for (int i = tid; i < D; i += NORM_THREADS) {
         float acc = 0.0f;
         for (int k = 0; k < K; ++k)
-            if (ok[k < 16 ? k : 15]) acc = __fmaf_rn(wk[k < 16 ? k : 15], eo[((int64_t)m * K + k) * D + i], acc);
+            if (ok[k < 16 ? k : 15]) acc = __fmaf_rn(wk[k < 16 ? k : 15], __ldcg(eo + ((int64_t)m * K + k) * D + i), acc);
         if (out) out[(int64_t)m * D + i] = acc;
         if (hr) {
             const float v = __fadd_rn(hr[i], acc);
@@ -844,10 +919,17 @@ cudaError_t kernels_configure() {
 
 cudaError_t launch_combine(const float *eo, const float *w, const int *sel, float scale, int M, int K,
                            int D, float *out, float *h, cudaStream_t st, const float *ln_w, float eps,
-                           float *hn) {
+                           float *hn, const EpWait *ep) {
     if (ln_w && (!h || !hn)) return cudaErrorInvalidValue;
+    EpWait none{};
     return launch_k(combine_kernel, dim3(M), dim3(NORM_THREADS), 0, st, eo, w, sel, scale, K, D, out, h, ln_w,
-                    eps, hn);
+                    eps, hn, ep ? *ep : none);
+}
+
+cudaError_t launch_ep_push(const EpPushParams &p, int nsm, cudaStream_t st) {
+    if (p.n < 1 || p.n > EP_MAX_RANKS || p.P < 1) return cudaErrorInvalidValue;
+    const int grid = p.P < 2 * nsm ? p.P : 2 * nsm;
+    return launch_k(ep_push_kernel, dim3(grid), dim3(256), 0, st, p);
 }
 
 cudaError_t launch_gemv_f32(const F32GemvParams &p, cudaStream_t st) {

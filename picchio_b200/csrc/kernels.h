@@ -92,13 +92,52 @@ cudaError_t launch_router(const RouterParams &r, cudaStream_t st);
 // Kernel attributes (shared-memory limits) once per device.
 cudaError_t kernels_configure();
 
+// ---- expert-parallel combine exchange ------------------------------------
+//
+// Under expert parallelism every rank holds every token's hidden row (the
+// dense part is replicated) and routes identically, so the dispatch side of
+// the MoE all-to-all needs no transfer: a rank's expert launches read their
+// (token, k) rows from its own copy.  The combine side moves bytes: each
+// (token, k) output row is computed on the rank owning that expert and is
+// needed by every rank.  ep_push writes this rank's rows straight into every
+// rank's receive buffer over NVLink (peer mappings of the other ranks'
+// exchange blocks) and then bumps, in every rank's flag array, this rank's
+// entry to the exchange number; the combine waits for all entries to reach
+// it before reading.  Receive buffers alternate with the exchange number, so
+// a rank that runs ahead writes the buffer its peers are not reading.
+constexpr int EP_MAX_RANKS = 8;
+constexpr int EP_FLAG_BYTES = 256;            // flag array at the start of each exchange block
+constexpr long long EP_WAIT_NS = 2000000000;  // bounded wait for the peers' rows (2 s)
+constexpr int EP_ERR_WAIT = 3;                // error word value when that wait gives up
+
+struct EpPushParams {
+    const float *eo;        // [P][D] this rank's expert outputs (rows of its own pairs)
+    const int *pair_local;  // [P] 1 where the pair's expert is on this rank
+    int P, D, rank, n;
+    char *blk[EP_MAX_RANKS];  // every rank's exchange block, mapped here
+    int64_t rx_bytes;         // bytes of one receive buffer
+    unsigned *state;          // this rank's [epoch, ticket]
+};
+cudaError_t launch_ep_push(const EpPushParams &p, int nsm, cudaStream_t st);
+
+// What the combine needs to read the exchanged rows (n = 0: no exchange,
+// eo is read as given).
+struct EpWait {
+    const char *blk;         // this rank's exchange block
+    int64_t rx_bytes;
+    const unsigned *state;   // this rank's epoch (the exchange to wait for)
+    int n;                   // ranks
+    int *err;                // error word: EP_ERR_WAIT when the wait gives up
+};
+
 // out[m][i] = sum over k (in k order) of w[m][k]*scale * eo[m*K+k][i]
 // (picchio.c:1445-1454); h[m][i] += out[m][i] when h != null.  With ln_w
 // (h required) hn[m] = rmsnorm(h[m] after the add, ln_w, eps), bit-equal to
-// launch_rmsnorm on that row.
+// launch_rmsnorm on that row.  With ep (n > 0) the rows come from the
+// exchange's receive buffer instead of eo, once every rank has pushed.
 cudaError_t launch_combine(const float *eo, const float *w, const int *sel, float scale, int M, int K,
                            int D, float *out, float *h, cudaStream_t st, const float *ln_w = nullptr,
-                           float eps = 0.0f, float *hn = nullptr);
+                           float eps = 0.0f, float *hn = nullptr, const EpWait *ep = nullptr);
 
 // y[m][o] = W[o] . x[m] for fp32 weights (matmul_f32, quant.h:117-148),
 // then (optional) + bias, and either stored, added to y (residual) or handed

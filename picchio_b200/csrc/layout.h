@@ -124,6 +124,10 @@ struct GemvParams {
     int stages;             // pipeline depth for this launch
     int stage_bytes;
     int static_jobs;        // 1: the job table does not depend on earlier kernels
+    int jobs_early;         // 1: the job table was written two or more kernels back (the down GEMV
+                            //    reads the router's): read through L2 before the dependency wait
+    int host_tiles;         // 1: some tiles may sit in mapped host memory (streamed residency): the
+                            //    weight rings use per-lane cp.async instead of bulk (TMA) copies
     // Shared input rows: > 0 means the B operand holds input rows
     // 0..shared_rows-1 for the whole launch (filled once per CTA) and a job's
     // in_row[r] is the B column of its row r.  0: per-job B (in_row = x row).

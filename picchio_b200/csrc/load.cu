@@ -417,6 +417,7 @@ pc_status alloc_runtime(pc_ctx *c) {
     c->err = c->d_next + M;
     PC_TRY(dalloc(c, M * 4, (void **)&c->d_seq_rows));
     PC_TRY(dalloc(c, M * 4, (void **)&c->d_seq_zero));
+    PC_TRY(dalloc(c, M * 4, (void **)&c->d_seq_one));
     std::vector<int> rows(M);
     for (int i = 0; i < M; ++i) rows[i] = i < c->nseq ? i : 0;
     PC_CU(cudaMemcpy(c->d_seq_rows, rows.data(), M * 4, cudaMemcpyHostToDevice));

@@ -364,7 +364,6 @@ pc_status run_moe_tc(pc_ctx *c, int l, const float *x, int M, float *out, float 
         t.swiglu_alpha = k.swiglu_alpha;
         PC_CU(tc_exp_launch(t, c->eg.gu.gs, c->e_hi - c->e_lo, P, c->st));
     }
-    if (ep) PC_CU(cudaMemsetAsync(c->eo, 0, (size_t)P * D * 4, c->st));
     {
         Prof pr(c, "expert_down");
         PC_CU(tc_exp_gather(c->tex, c->act, k.intermediate, k.intermediate, K, true, c->pair_start, c->pair_list,
@@ -376,9 +375,17 @@ pc_status run_moe_tc(pc_ctx *c, int l, const float *x, int M, float *out, float 
         PC_CU(tc_exp_launch(t, c->eg.dn.gs, c->e_hi - c->e_lo, P, c->st));
     }
     c->launches += 4;
-    if (ep) PC_TRY(ep_allreduce_sum(c, c->eo, (size_t)P * D));
-    PC_CU(launch_combine(c->eo, c->rw, layer_sel(c, l), k.routed_scale, M, K, D, out, h, c->st, next_ln, k.eps,
-                         c->hn));
+    EpWait ew{};
+    if (ep) {
+        Prof pr(c, "ep_exchange");
+        PC_TRY(ep_exchange(c, P));
+        ew = ep_wait_view(c);
+    }
+    {
+        Prof pr(c, "combine");
+        PC_CU(launch_combine(c->eo, c->rw, layer_sel(c, l), k.routed_scale, M, K, D, out, h, c->st, next_ln,
+                             k.eps, c->hn, &ew));
+    }
     ++c->launches;
     return PC_OK;
 }
@@ -464,6 +471,7 @@ pc_status run_moe(pc_ctx *c, int l, const float *x, int M, const int *sel_in, co
     GemvParams p{};
     params_for(p, c->eg.gu, EPI_SWIGLU);
     p.static_jobs = 0;  // written by the router kernel
+    p.host_tiles = c->res.on ? 1 : 0;  // streamed residency: a job may read a pinned host copy
     p.jobs = c->jobs_gu;
     p.njobs = c->njobs;
     p.x = x;
@@ -475,9 +483,10 @@ pc_status run_moe(pc_ctx *c, int l, const float *x, int M, const int *sel_in, co
     p.shared_rows = shared_rows_for(M);  // B column = token row
     PC_TRY(run_gemv(c, p, rows, "expert_gate_up"));
     const bool ep = c->nccl_comm != nullptr;
-    if (ep) PC_CU(cudaMemsetAsync(c->eo, 0, (size_t)M * K * D * 4, c->st));
     params_for(p, c->eg.dn, EPI_STORE);
     p.static_jobs = 0;
+    p.jobs_early = 1;  // written by the router, two launches back: weights stream before the wait
+    p.host_tiles = c->res.on ? 1 : 0;
     p.jobs = c->jobs_dn;
     p.njobs = c->njobs + 1;
     p.x = c->act;
@@ -488,7 +497,12 @@ pc_status run_moe(pc_ctx *c, int l, const float *x, int M, const int *sel_in, co
     // expert's job fills B with just its own rows
     p.shared_rows = gemv_nt_for_rows(M * K) == 1 ? M * K : 0;
     PC_TRY(run_gemv(c, p, rows, "expert_down"));
-    if (ep) PC_TRY(ep_allreduce_sum(c, c->eo, (size_t)M * K * D));
+    EpWait ew{};
+    if (ep) {
+        Prof pr(c, "ep_exchange");
+        PC_TRY(ep_exchange(c, M * K));
+        ew = ep_wait_view(c);
+    }
     if (c->trace) {
         const int last = M - 1;
         for (int kk = 0; kk < K; ++kk) {
@@ -498,8 +512,11 @@ pc_status run_moe(pc_ctx *c, int l, const float *x, int M, const int *sel_in, co
                       c->eo + ((size_t)last * K + kk) * D, D);
         }
     }
-    PC_CU(launch_combine(c->eo, c->rw, layer_sel(c, l), k.routed_scale, M, K, D, out, h, c->st, next_ln, k.eps,
-                         c->hn));
+    {
+        Prof pr(c, "combine");
+        PC_CU(launch_combine(c->eo, c->rw, layer_sel(c, l), k.routed_scale, M, K, D, out, h, c->st, next_ln,
+                             k.eps, c->hn, &ew));
+    }
     ++c->launches;
     return PC_OK;
 }
@@ -1028,9 +1045,22 @@ pc_status pc_decode_batch(pc_ctx *c, const int *toks, const int *pos, int B, int
 }
 
 pc_status pc_prefill(pc_ctx *c, const int *ids, int n, int pos_base, int *next_tok) {
+    return pc_prefill_seq(c, 0, ids, n, pos_base, next_tok);
+}
+
+pc_status pc_prefill_seq(pc_ctx *c, int seq, const int *ids, int n, int pos_base, int *next_tok) {
     PC_TRY(check_ctx(c));
     if (!ids || !next_tok || n < 1) return fail(PC_ERR_INVALID_ARG, "empty prompt");
     if (pos_base < 0 || pos_base + n > c->kv_ctx) return fail(PC_ERR_RANGE, "prompt does not fit the KV capacity");
+    if (seq < 0 || seq >= c->nseq) return fail(PC_ERR_RANGE, "sequence slot outside [0, max_batch)");
+    if (seq != 0 && c->smp.on) return fail(PC_ERR_STATE, "device sampling serves sequence 0 only");
+    const int *seq_rows = c->d_seq_zero;  // every row of the step in slot seq
+    if (seq != 0) {
+        std::vector<int> sv(c->maxm, seq);
+        PC_CU(cudaMemcpyAsync(c->d_seq_one, sv.data(), sv.size() * 4, cudaMemcpyHostToDevice, c->st));
+        PC_CU(cudaStreamSynchronize(c->st));
+        seq_rows = c->d_seq_one;
+    }
     // with device sampling the blocks are the reference's 64 positions (each
     // draws); otherwise opts.prefill_chunk positions per step
     const int chunk = std::min(c->maxm, c->smp.on ? 64 : std::max(1, c->opts.prefill_chunk));
@@ -1046,7 +1076,7 @@ pc_status pc_prefill(pc_ctx *c, const int *ids, int n, int pos_base, int *next_t
         const bool lm = off + m >= n || c->smp.on;
         DenseJobs *dj = nullptr;
         PC_TRY(dense_jobs(c, m, lm ? 1 : 2, &dj));
-        PC_TRY(run_step(c, m, c->d_seq_zero, lm ? 1 : 2, split_bucket(c, ps[m - 1]), dj));
+        PC_TRY(run_step(c, m, seq_rows, lm ? 1 : 2, split_bucket(c, ps[m - 1]), dj));
         PC_CU(cudaStreamSynchronize(c->st));
         PC_TRY(res_after_step(c));
     }

@@ -219,6 +219,46 @@ def make_gptoss(threads=8):
     print("gptoss_2l ids", ids[:12], "... long", long_ids)
 
 
+def make_gptoss_bf16kv():
+    """gptoss_2l_bf16kv.npz: the same calls as make_gptoss on the oracle with
+    a bf16 KV cache (OracleModel(kv_bf16=True): every stored K/V row rounded
+    to bf16, the device's cache format; the rest is the oracle restatement
+    pinned bit-exact to the reference).  Teacher-forced on the reference's
+    ids, as the device test runs; the GPTOSS_PROBE_KEYS stage tensors at the
+    probe calls, every stage tensor of the last call, and of the last call
+    after the long prompt."""
+    with open(os.path.join(HERE, "gptoss_2l.json")) as f:
+        meta = json.load(f)
+    cfg = SynthConfig(**GPTOSS)
+    arrays = {}
+    with tempfile.TemporaryDirectory() as d:
+        make_model(d, cfg, GPTOSS_SEED)
+        m = O.OracleModel(d, ctx=meta["ctx"], kv_bf16=True)
+        prompt, ids = meta["prompt"], meta["ids"]
+        for i, t in enumerate(prompt):
+            m.forward_token(t, i)
+        for s in range(1, GPTOSS_STEPS + 1):
+            m.forward_token(ids[s - 1], len(prompt) + s - 1)
+            if s in GPTOSS_PROBES:
+                for k in GPTOSS_PROBE_KEYS:
+                    arrays[f"probe{s}.{k}"] = m.dumps[k].reshape(-1).astype(np.float32)
+            if s == GPTOSS_STEPS:
+                for k, v in m.dumps.items():
+                    if STAGE_RE.match(k):
+                        arrays[f"last.{k}"] = np.asarray(v).reshape(-1).astype(np.float32)
+        m = O.OracleModel(d, ctx=meta["ctx"], kv_bf16=True)
+        lp, lids = meta["long_prompt"], meta["long_ids"]
+        for i, t in enumerate(lp):
+            m.forward_token(t, i)
+        for s in range(1, GPTOSS_LONG_STEPS + 1):
+            m.forward_token(lids[s - 1], len(lp) + s - 1)
+        for k, v in m.dumps.items():
+            if STAGE_RE.match(k):
+                arrays[f"long.{k}"] = np.asarray(v).reshape(-1).astype(np.float32)
+    np.savez_compressed(os.path.join(HERE, "gptoss_2l_bf16kv.npz"), **arrays)
+    print("gptoss_2l_bf16kv", len(arrays), "arrays")
+
+
 # The reference's command-line contract on the tiny model: a SERVICE=1
 # session (service_loop, picchio.c:2700-2795) with prefix reuse (TURN keep),
 # greedy and sampled turns, the range and vocabulary errors, RESET and
@@ -276,5 +316,7 @@ if __name__ == "__main__":
         make_kernels()
     if "gptoss" in which:
         make_gptoss()
+    if "gptoss" in which or "gptoss_bf16kv" in which:
+        make_gptoss_bf16kv()
     if "service" in which:
         make_service()

@@ -1,18 +1,21 @@
-"""Expert parallelism, host side, on CPU with two gloo ranks.
+"""Expert parallelism, host side, on CPU with gloo ranks.
 
 The device path shards the experts of every layer over the ranks with the
 rule used by ``pc_init`` (model.cu): rank r of n holds experts
 [E*r/n, E*(r+1)/n).  Attention, router and lm_head are replicated, so every
-rank routes identically.  After the down projection a rank holds the outputs
-of its own (token, k) pairs and zeros elsewhere; one all-reduce (sum) gives
-every rank all pair outputs, and the weighted combine then runs in k order,
-as moe_forward does (picchio.c:1445-1454).  Each element has exactly one
-nonzero contributor, so the exchange is exact.
+rank holds every token's hidden row and routes identically: the dispatch
+side of the MoE all-to-all needs no transfer.  After the down projection a
+rank holds the output rows of its own (token, k) pairs; the combine exchange
+sends exactly those rows to every other rank (ep_push writes them into the
+other GPUs' receive buffers), each rank knowing from the shared routing
+which rows arrive from whom.  The weighted combine then runs in k order, as
+moe_forward does (picchio.c:1445-1454), so the result is bit-identical to
+one process.
 
-These tests run that exchange with the oracle's expert arithmetic on two
-``gloo`` ranks and require the result to be bit-identical to the
-single-process moe_forward.  They also cover a rank that fails before the
-exchange: the other rank must get an error from the process group's timeout
+These tests run that exchange with the oracle's expert arithmetic on gloo
+ranks (point-to-point sends of the owned rows only) and require the
+single-process moe_forward's bits.  They also cover a rank that fails before
+the exchange: the others must get an error from the process group's timeout
 instead of waiting forever.
 """
 import datetime
@@ -64,16 +67,30 @@ def _moe_rank(rank, world, port, model_dir, xs, out_path, fail_rank):
             for l in range(c.n_layers):
                 ly = m.layers[l]
                 _, sel, wts = O.router_topk(x, ly["router"], ly["router_bias"], c.topk, bias_first=False)
-                eo = np.zeros((c.topk, c.hidden), np.float32)
+                ranges = [expert_range(c.n_experts, q, world) for q in range(world)]
+                owner = [next(q for q, (a, b) in enumerate(ranges) if a <= int(e) < b) for e in sel]
+                eo = np.full((c.topk, c.hidden), np.nan, np.float32)
                 for k, e in enumerate(sel):
                     if lo <= int(e) < hi:
                         gu, dn, gub, db = m.expert(l, int(e))
                         g = (gu.matmul(x)[0] + gub).astype(np.float32)
                         act = O.swiglu(g, c.swiglu_limit, c.swiglu_alpha)
                         eo[k] = (dn.matmul(act)[0] + db).astype(np.float32)
-                t = torch.from_numpy(eo)
-                dist.all_reduce(t, op=dist.ReduceOp.SUM)
-                eo = t.numpy()
+                # combine exchange: my rows to every other rank, theirs to me
+                reqs, recv = [], {}
+                for k in range(c.topk):
+                    if owner[k] == rank:
+                        for q in range(world):
+                            if q != rank:
+                                reqs.append(dist.isend(torch.from_numpy(eo[k].copy()), q, tag=k))
+                    else:
+                        recv[k] = torch.empty(c.hidden, dtype=torch.float32)
+                        reqs.append(dist.irecv(recv[k], owner[k], tag=k))
+                for rq in reqs:
+                    rq.wait()
+                for k, t in recv.items():
+                    eo[k] = t.numpy()
+                assert not np.isnan(eo).any()
                 out = np.zeros(c.hidden, np.float32)
                 for k in range(c.topk):
                     w = np.float32(np.float32(wts[k]) * c.routed_scale)
@@ -98,8 +115,9 @@ def _run(world, fail_rank=-1):
     return tmp, xs, np.load(out_path)
 
 
-def test_ep_allreduce_combine_is_exact():
-    tmp, xs, got = _run(2)
+@pytest.mark.parametrize("world", [2, 4])
+def test_ep_combine_exchange_is_exact(world):
+    tmp, xs, got = _run(world)
     m = O.OracleModel(tmp)
     ref = []
     for x in xs:

@@ -11,10 +11,16 @@ last call.
 
 Bars: greedy ids identical, router top-k identical,
 per-layer hidden states within 1e-2 relative L2.  With the reference's fp32
-KV cache the hidden states are also held to 1e-5.  The bf16 KV cache stores
-K and V rounded to bf16 (2^-9 relative), so its decode is teacher-forced on
-the reference's ids: each call must still pick the reference's next id and
-top-k, the hidden states within 1e-2.
+KV cache the hidden states are also held to 1e-4 (the GEMVs round each
+input row to 22 significant bits; measured errors stay near 1e-5).
+
+The bf16 KV cache stores K and V rounded to bf16 (2^-9 relative).  On this
+random-weight model that alone moves the hidden states by up to ~1.8 %
+from the reference's fp32-cache values (the oracle with the same rounding,
+OracleModel(kv_bf16=True), shows the same gap), so the bf16 decode is
+teacher-forced on the reference's ids: each call must still pick the
+reference's next id and top-k, and every stage tensor must match the bf16
+oracle's (gptoss_2l_bf16kv.npz) within 1e-3.
 """
 import json
 import os
@@ -26,7 +32,8 @@ from picchio_b200.synth import SynthConfig, make_model
 
 GOLD = os.path.join(os.path.dirname(__file__), "golden")
 HIDDEN_REL_L2 = 1e-2
-FP32_KV_REL_L2 = 1e-5
+FP32_KV_REL_L2 = 1e-4
+BF16_KV_REL_L2 = 1e-3
 
 pytestmark = pytest.mark.gpu
 
@@ -45,6 +52,12 @@ def gold():
 
 
 @pytest.fixture(scope="module")
+def gold_bf16():
+    """The bf16-KV oracle's stage tensors for the same (teacher-forced) calls."""
+    return np.load(os.path.join(GOLD, "gptoss_2l_bf16kv.npz"))
+
+
+@pytest.fixture(scope="module")
 def model_dir(gold, tmp_path_factory):
     meta, _ = gold
     d = str(tmp_path_factory.mktemp("gptoss_2l"))
@@ -52,8 +65,10 @@ def model_dir(gold, tmp_path_factory):
     return d
 
 
-def _stage_checks(model, dumps, prefix, names, bar):
-    """Compares traced stage tensors with the reference's; returns the count."""
+def _stage_checks(model, dumps, prefix, names, bar, hidden_only=True):
+    """Compares traced stage tensors with the golden ones; returns the count.
+    Every tensor within HIDDEN_REL_L2 and the hidden states (or, with
+    hidden_only False, all of them) within bar; top-k indices identical."""
     n = 0
     for name in names:
         ref = dumps[prefix + name]
@@ -63,14 +78,15 @@ def _stage_checks(model, dumps, prefix, names, bar):
         else:
             err = rel_l2(got, ref)
             assert err < HIDDEN_REL_L2, (prefix, name, err)
-            if name.endswith((".input", ".output", "final_norm", "pre_moe_norm", "pre_attn_norm")):
+            if not hidden_only or name.endswith((".input", ".output", "final_norm", "pre_moe_norm",
+                                                 "pre_attn_norm")):
                 assert err < bar, (prefix, name, err)
         n += 1
     return n
 
 
 @pytest.mark.parametrize("kv_bf16", [False, True], ids=["fp32_kv", "bf16_kv"])
-def test_decode_against_reference(gold, model_dir, kv_bf16):
+def test_decode_against_reference(gold, gold_bf16, model_dir, kv_bf16):
     """Prefill of 120 ids, then 143 decode calls (positions 120..262) on the
     fast path (CUDA graphs; with the bf16 cache the tensor-core attention):
     the next id and the router top-k of both layers at every call; traced
@@ -79,7 +95,8 @@ def test_decode_against_reference(gold, model_dir, kv_bf16):
     meta, dumps = gold
     ids, topk, probes = meta["ids"], meta["top_indices"], set(meta["probes"])
     P = len(meta["prompt"])
-    bar = 1.0 if kv_bf16 else FP32_KV_REL_L2
+    bar = BF16_KV_REL_L2 if kv_bf16 else FP32_KV_REL_L2
+    stages = gold_bf16 if kv_bf16 else dumps
     last_names = [k[len("last."):] for k in dumps.files if k.startswith("last.")]
     with Model(model_dir, ctx=meta["ctx"], kv_bf16=kv_bf16) as m:
         tok = m.prefill_tokens(meta["prompt"], 0)
@@ -99,14 +116,14 @@ def test_decode_against_reference(gold, model_dir, kv_bf16):
                 assert m.forward_token(tok_in, pos) == tok
                 names = last_names if s == meta["steps"] else meta["probe_keys"]
                 prefix = "last." if s == meta["steps"] else f"probe{s}."
-                n_stage += _stage_checks(m, dumps, prefix, names, bar)
+                n_stage += _stage_checks(m, stages, prefix, names, bar, hidden_only=not kv_bf16)
                 m.set_trace(False)
         assert n_stage >= 60
 
 
 @pytest.mark.parametrize("chunk", [64, 1024])
 @pytest.mark.parametrize("kv_bf16", [False, True], ids=["fp32_kv", "bf16_kv"])
-def test_long_prefill_against_reference(gold, model_dir, chunk, kv_bf16):
+def test_long_prefill_against_reference(gold, gold_bf16, model_dir, chunk, kv_bf16):
     """A 300-id prompt in 64-position steps (GEMV experts) and in one
     300-position step (1200 routed pairs: expert GEMMs on tcgen05, dense
     projections on tcgen05), then 8 greedy calls; the stage tensors of the
@@ -127,8 +144,12 @@ def test_long_prefill_against_reference(gold, model_dir, chunk, kv_bf16):
             got.append(tok)
             pos += 1
         assert got[:len(want)] == want
-        tol = 1.0 if kv_bf16 else (2e-3 if chunk > 64 else FP32_KV_REL_L2)
-        assert _stage_checks(m, dumps, "long.", names, tol) >= 40
+        if kv_bf16:  # against the bf16-KV oracle; f16 expert operands at chunk 1024
+            tol = 3e-3 if chunk > 64 else BF16_KV_REL_L2
+            assert _stage_checks(m, gold_bf16, "long.", names, tol, hidden_only=False) >= 40
+        else:
+            tol = 2e-3 if chunk > 64 else FP32_KV_REL_L2
+            assert _stage_checks(m, dumps, "long.", names, tol) >= 40
 
 
 @pytest.mark.parametrize("M", [1, 4, 64, 512])

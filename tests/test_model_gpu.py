@@ -122,6 +122,29 @@ def test_decode_batch_matches_single_sequences(variant):
             assert outs[i] == singles[i][:6] or outs[i][:len(singles[i])] == singles[i][:len(outs[i])]
 
 
+def test_prefill_into_slots_then_batch_decode(variant):
+    """pc_prefill_seq fills KV slots 1 and 2 of a batched context with their
+    own prompts; pc_decode_batch then continues each slot as the
+    single-sequence prefill + decode does (same ids)."""
+    from picchio_b200 import Model
+    m, d = variant
+    prompts = [m["prompt"][:12], m["prompt"][12:31], m["prompt"][31:40]]
+    singles = []
+    for p in prompts:
+        with Model(d, ctx=m["ctx"]) as s:
+            singles.append(s.generate(p, 5))
+    with Model(d, ctx=m["ctx"], max_batch=3) as b:
+        cur = [b.prefill_tokens(p, 0, seq=i) for i, p in enumerate(prompts)]
+        pos = [len(p) for p in prompts]
+        outs = [[c] for c in cur]
+        for _ in range(4):
+            cur = b.decode_batch(cur, pos)
+            pos = [q + 1 for q in pos]
+            for i in range(3):
+                outs[i].append(cur[i])
+    assert outs == singles
+
+
 def test_decode_batch_tensor_core_rows(variant):
     """18 sequences in one batch: q/k/v, o_proj and the lm_head of every step
     take the tensor-core path (16..128 rows); each sequence's greedy ids match
