@@ -50,8 +50,13 @@ typedef enum {
 typedef struct pc_ctx pc_ctx;
 typedef struct pc_qt pc_qt;
 
-/* Weight formats, as quant.h:32-41 numbers them (QT.fmt). */
-enum { PC_FMT_F32 = 0, PC_FMT_INT8 = 1, PC_FMT_INT4 = 2 };
+/* Weight formats, as quant.h:32-41 numbers them (QT.fmt).  PC_FMT_MXFP4 is
+ * the reference's fmt 3 (OCP MXFP4: E2M1 codes two per byte, low nibble =
+ * even column, one scale per 32 columns), which the reference declares but
+ * converts to INT4 at build time (quant.h:334-336, convert.py:391-447); here
+ * it runs natively, value = E2M1(code) * scale as convert.py:129-178
+ * dequantizes it. */
+enum { PC_FMT_F32 = 0, PC_FMT_INT8 = 1, PC_FMT_INT4 = 2, PC_FMT_MXFP4 = 3 };
 
 typedef struct {
     int device;        /* CUDA device ordinal */
@@ -93,6 +98,8 @@ typedef struct {
     int attn_format;     /* PC_FMT_* of q/k/v/o */
     int attn_group_size; /* group size when attn_format == PC_FMT_INT4 */
     int layer_type[256]; /* 0 sliding, 1 full (picchio.c:389-409) */
+    int expert_format;   /* PC_FMT_INT4 (0 also means INT4) or PC_FMT_MXFP4 (group size 32): what
+                            pc_init_synthetic generates; pc_init sets it from the experts it loads */
 } pc_model_cfg;
 
 /* Fills *o with the defaults (device 0, ctx 512, fp32 KV, batch 1, graphs on,
@@ -251,7 +258,9 @@ pc_status pc_expert_stats(pc_ctx *ctx, uint64_t *hits, uint64_t *misses, uint64_
  * fmt PC_FMT_F32: data = float[O*I]; PC_FMT_INT8: data = int8[O*I], scales =
  * float[O]; PC_FMT_INT4: data = packed nibbles [O][ceil(I/2)] (low nibble =
  * even column, value = nibble - 8), scales = float[O] (block_size 0) or
- * float[O][ceil(I/gs)] (block_size = gs). */
+ * float[O][ceil(I/gs)] (block_size = gs); PC_FMT_MXFP4: data = packed E2M1
+ * codes in the same layout, block_size 32, scales = float[O][ceil(I/32)]
+ * (the decoded E8M0 factors, 2^(e - 127)). */
 pc_status pc_qt_create(int device, int fmt, int O, int I, int block_size, const void *data,
                        const float *scales, pc_qt **out);
 /* y_dev[S][O] = x_dev[S][I] . W^T on `stream` (a cudaStream_t, NULL = default). */

@@ -394,6 +394,25 @@ def _load_qt(t: dict, name: str, O: int, I: int) -> QT:
     raise ValueError(f"{name}: dtype {dt} not handled by the oracle")
 
 
+# E2M1 values of the 16 codes (convert.py:98-103), code 8 is -0.0
+FP4_LUT = np.array([0.0, 0.5, 1.0, 1.5, 2.0, 3.0, 4.0, 6.0,
+                    -0.0, -0.5, -1.0, -1.5, -2.0, -3.0, -4.0, -6.0], np.float32)
+
+
+def dequant_mxfp4(packed, e8m0, O, I):
+    """MXFP4 -> fp32 exactly as convert.py dequantizes it before its INT4
+    requantization (convert.py:413-431, decode_e8m0 convert.py:129-134):
+    two codes per byte (low nibble = even column), value = FP4_LUT[code] *
+    2^(e - 127) as one float32 multiply."""
+    b = np.asarray(packed, np.uint8).reshape(O, I // 2)
+    codes = np.empty((O, I), np.uint8)
+    codes[:, 0::2] = b & 0x0F
+    codes[:, 1::2] = b >> 4
+    vals = FP4_LUT[codes]
+    sc = np.ldexp(np.ones((O, I // 32), np.float32), np.asarray(e8m0).reshape(O, I // 32).astype(np.int32) - 127)
+    return (vals * np.repeat(sc.astype(np.float32), 32, axis=1)).astype(np.float32)
+
+
 def bf16_round(a):
     """fp32 -> bf16 -> fp32 with round-to-nearest-even (what the device's
     __float2bfloat16_rn stores), for finite values."""
@@ -455,11 +474,24 @@ class OracleModel:
         self.dumps: dict = {}
 
     def expert(self, l: int, e: int):
-        """(gate_up QT, down QT, gu_bias, d_bias) as expert_load gives them (picchio.c:698-888)."""
+        """(gate_up QT, down QT, gu_bias, d_bias) as expert_load gives them
+        (picchio.c:698-888).  Experts in the checkpoint's MXFP4 form
+        (``<proj>_blocks`` / ``<proj>_scales``, which the reference only
+        reaches after convert.py turns them into INT4) are dequantized as
+        convert.py does and applied with the reference's fp32 matmul
+        (matmul_f32, quant.h:117-148): the reference's fmt 3 semantics."""
         ly = self.layers[l]
         if e not in ly["experts"]:
             c, t = self.c, self.t
             p = f"model.layers.{l}.mlp.experts."
+            if (p + "gate_up_proj_blocks") in t:
+                def mx(which, O, I):
+                    blk, sc = t[p + which + "_blocks"][1], t[p + which + "_scales"][1]
+                    return QT(0, O, I, dequant_mxfp4(blk[e], sc[e], O, I))
+                gu = mx("gate_up_proj", c.moe_inter, c.hidden)
+                dn = mx("down_proj", c.hidden, c.moe_inter // 2)
+                ly["experts"][e] = (gu, dn, ly["gu_bias"][e], ly["d_bias"][e])
+                return ly["experts"][e]
             gu = _load_qt(t, p + f"gate_up_proj.{e}", c.moe_inter, c.hidden)
             dn = _load_qt(t, p + f"down_proj.{e}", c.hidden, c.moe_inter // 2)
             ly["experts"][e] = (gu, dn, ly["gu_bias"][e], ly["d_bias"][e])

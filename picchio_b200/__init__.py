@@ -7,5 +7,5 @@ library is missing or no CUDA device is present, calls raise.
 """
 from .api import (  # noqa: F401
     PicchioError, Model, ModelConfig, QT, nccl_unique_id, lib, LIB_PATH,
-    FMT_F32, FMT_INT8, FMT_INT4,
+    FMT_F32, FMT_INT8, FMT_INT4, FMT_MXFP4,
 )

@@ -18,7 +18,7 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "libpicchio_b200.so")
 
-FMT_F32, FMT_INT8, FMT_INT4 = 0, 1, 2
+FMT_F32, FMT_INT8, FMT_INT4, FMT_MXFP4 = 0, 1, 2, 3
 
 STATUS = ["PC_OK", "PC_ERR_INVALID_ARG", "PC_ERR_IO", "PC_ERR_FORMAT", "PC_ERR_MISSING_TENSOR",
           "PC_ERR_CUDA", "PC_ERR_OOM", "PC_ERR_RANGE", "PC_ERR_TIMEOUT", "PC_ERR_NCCL", "PC_ERR_STATE"]
@@ -45,7 +45,7 @@ class _Cfg(C.Structure):
                 ("routed_scale", C.c_float), ("rope_factor", C.c_float), ("rope_beta_fast", C.c_float),
                 ("rope_beta_slow", C.c_float), ("rope_original_ctx", C.c_int), ("rope_truncate", C.c_int),
                 ("group_size", C.c_int), ("attn_format", C.c_int), ("attn_group_size", C.c_int),
-                ("layer_type", C.c_int * 256)]
+                ("layer_type", C.c_int * 256), ("expert_format", C.c_int)]
 
 
 @dataclass
@@ -76,6 +76,7 @@ class ModelConfig:
     attn_format: int = FMT_INT8
     attn_group_size: int = 0
     layer_types: list = field(default_factory=list)  # default: alternate sliding/full
+    expert_format: int = FMT_INT4  # FMT_MXFP4: experts as MXFP4 (group size 32)
 
     @staticmethod
     def gpt_oss_20b(**kw) -> "ModelConfig":

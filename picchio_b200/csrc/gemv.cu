@@ -28,6 +28,7 @@ cudaError_t go(const GemvParams &p, int grid, size_t smem, cudaStream_t st) {
 template <int NT>
 cudaError_t go_nt(const GemvParams &p, int grid, size_t smem, cudaStream_t st) {
     if (p.fmt == TF_T8) return go<TF_T8, NT, 0>(p, grid, smem, st);
+    if (p.fmt == TF_F4) return p.gs == 32 ? go<TF_F4, NT, 32>(p, grid, smem, st) : cudaErrorInvalidValue;
     switch (p.gs) {
         case 32: return go<TF_T4, NT, 32>(p, grid, smem, st);
         case 64: return go<TF_T4, NT, 64>(p, grid, smem, st);
@@ -44,6 +45,7 @@ cudaError_t set_nt(int max_smem) {
     if (e == cudaSuccess) e = set_smem<TF_T4, NT, 16>(max_smem);
     if (e == cudaSuccess) e = set_smem<TF_T4, NT, 32>(max_smem);
     if (e == cudaSuccess) e = set_smem<TF_T4, NT, 64>(max_smem);
+    if (e == cudaSuccess) e = set_smem<TF_F4, NT, 32>(max_smem);
     return e;
 }
 

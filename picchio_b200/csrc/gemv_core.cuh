@@ -152,7 +152,7 @@ __device__ __forceinline__ float pow2i(int e) { return __int_as_float((e + 127) 
 // each thread rounds 8 values of one row for one lane column t and
 // writes the 4 digit lanes of that row, four items per round so their loads
 // overlap.
-template <int NT, int CPB>
+template <int NT, int CPB, int INV>
 __device__ void fill_B(const GemvParams &p, const int *rows, int n, SMeta *meta, int mb, uint2 *Bsm,
                        int cw, int lane, int ctid) {
     const int nrows = min(n, NT * 2);
@@ -243,7 +243,7 @@ __device__ void fill_B(const GemvParams &p, const int *rows, int n, SMeta *meta,
             if (ctid == r && r < nrows) {
                 meta->scale[mb][r] = pow2i(sh[r]);
                 // removes 2^sh and, for INT4, the factor 16 of the s8 nibble values
-                meta->inv[mb][r] = ldexpf(1.0f, -sh[r] - (CPB == 2 ? 4 : 0));
+                meta->inv[mb][r] = ldexpf(1.0f, -sh[r] - INV);
             }
 #pragma unroll
         for (int q = 0; q < IPT; ++q) {
@@ -282,7 +282,7 @@ __device__ void fill_B(const GemvParams &p, const int *rows, int n, SMeta *meta,
     if (ctid < nrows) {
         const int sh = scale_of(ctid);
         meta->scale[mb][ctid] = pow2i(sh);
-        meta->inv[mb][ctid] = ldexpf(1.0f, -sh - (CPB == 2 ? 4 : 0));
+        meta->inv[mb][ctid] = ldexpf(1.0f, -sh - INV);
     }
     // pass 2: each thread rounds four items per round so their loads overlap
     for (int base = ctid; base < total; base += 4 * NCT) {
@@ -310,7 +310,7 @@ template <int FMT, int GS>
 __device__ __forceinline__ void load_blk(BlkRegs &r, const uint8_t *blk, int lane) {
     const int g = lane >> 2;
     r.a = ldg_stream(blk + lane * 16);
-    if (FMT == TF_T4 && GS == 32) {
+    if (tf_4bit(FMT) && GS == 32) {
         r.s = ldg_stream(blk + 512 + g * 16);
     } else if (FMT == TF_T4 && GS == 64) {
         const uint2 v = ldg_stream2(blk + 512 + g * 8);
@@ -336,7 +336,7 @@ template <int FMT, int GS>
 __device__ __forceinline__ void load_blk_smem(BlkRegs &r, const uint8_t *blk, int lane) {
     const int g = lane >> 2;
     r.a = *reinterpret_cast<const uint4 *>(blk + lane * 16);
-    if (FMT == TF_T4 && GS == 32) {
+    if (tf_4bit(FMT) && GS == 32) {
         r.s = *reinterpret_cast<const uint4 *>(blk + 512 + g * 16);
     } else if (FMT == TF_T4 && GS == 64) {
         const uint2 v = *reinterpret_cast<const uint2 *>(blk + 512 + g * 8);
@@ -352,12 +352,35 @@ __device__ __forceinline__ void load_blk_smem(BlkRegs &r, const uint8_t *blk, in
 // each group's sum is exact in s32 and is scaled into the fp32 accumulator
 // acc, the structure of matmul_i4_gs (quant.h:259-319); per-row scale (GS 0):
 // sums stay in the s32 accumulator ia.
-template <int NT, int GS>
+// Four E2M1 codes (bits 0-15 of s, code j in bits 4j..4j+3) -> four signed
+// bytes holding 2x their values: byte permutes into the magnitude table
+// {0, 1, 2, 3, 4, 6, 8, 12} and its negation, then a permute picking, per
+// byte, the one the code's sign bit names (so code 8, -0, gives 0).
+__device__ __forceinline__ uint32_t e2m1x4_s8(uint32_t s) {
+    const uint32_t idx = s & 0x7777u;
+    const uint32_t mag = prmt(0x03020100u, 0x0C080604u, idx);
+    const uint32_t neg = prmt(0xFDFEFF00u, 0xF4F8FAFCu, idx);
+    return prmt(mag, neg, ((s >> 1) & 0x4444u) | 0x3210u);
+}
+
+// The A fragments of one 4-bit block for the two MMA steps: INT4 nibbles n
+// become 16 (n - 8); MXFP4 codes become 2 x their E2M1 value.
+template <int FMT>
+__device__ __forceinline__ void a_frags4(const uint4 &a, uint32_t (&a0)[4], uint32_t (&a1)[4]) {
+    if (FMT == TF_F4) {
+        a0[0] = e2m1x4_s8(a.x); a0[1] = e2m1x4_s8(a.x >> 16); a0[2] = e2m1x4_s8(a.y); a0[3] = e2m1x4_s8(a.y >> 16);
+        a1[0] = e2m1x4_s8(a.z); a1[1] = e2m1x4_s8(a.z >> 16); a1[2] = e2m1x4_s8(a.w); a1[3] = e2m1x4_s8(a.w >> 16);
+    } else {
+        a0[0] = nib_lo_s8(a.x); a0[1] = nib_hi_s8(a.x); a0[2] = nib_lo_s8(a.y); a0[3] = nib_hi_s8(a.y);
+        a1[0] = nib_lo_s8(a.z); a1[1] = nib_hi_s8(a.z); a1[2] = nib_lo_s8(a.w); a1[3] = nib_hi_s8(a.w);
+    }
+}
+
+template <int FMT, int NT, int GS>
 __device__ __forceinline__ void block_t4(const BlkRegs &r, const uint4 (&B)[NT], float (&acc)[NT][4],
                                          int (&ia)[NT][4]) {
     uint32_t a0[4], a1[4];
-    a0[0] = nib_lo_s8(r.a.x); a0[1] = nib_hi_s8(r.a.x); a0[2] = nib_lo_s8(r.a.y); a0[3] = nib_hi_s8(r.a.y);
-    a1[0] = nib_lo_s8(r.a.z); a1[1] = nib_hi_s8(r.a.z); a1[2] = nib_lo_s8(r.a.w); a1[3] = nib_hi_s8(r.a.w);
+    a_frags4<FMT>(r.a, a0, a1);
     const int M[4] = {0, 0, 0, 0};
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
@@ -556,14 +579,17 @@ __device__ __forceinline__ int job_of(const int *jp, int u, int j) {
 
 constexpr int BAR_FILL = 1;  // named barrier 1: all threads (B refills); 2..15: group reductions
 
-// FMT: TF_T4 / TF_T8; NT: 1 or 2 N-tiles (<= 4 or <= 8 input rows); GS:
+// FMT: TF_T4 / TF_F4 / TF_T8; NT: 1 or 2 N-tiles (<= 4 or <= 8 input rows); GS:
 // INT4 group size (0 = per row).
 // The GEMV work of one CTA (index cta of ncta) over the job list of p.  PDL:
 // the launch is a programmatic dependent launch (gemv_kernel); MBX > 0
 // overrides the blocks per ring step.
 template <int FMT, int NT, int GS, bool PDL, int MBX = 0>
 __device__ __forceinline__ void gemv_cta(const GemvParams &p, uint8_t *smem, int cta, int ncta) {
-    constexpr int CPB = FMT == TF_T4 ? 2 : 1;  // 32-column MMA steps per block
+    constexpr int CPB = tf_4bit(FMT) ? 2 : 1;  // 32-column MMA steps per block
+    // weight values in the MMA are 16 (n - 8) for INT4 and 2 x E2M1 for MXFP4:
+    // the extra power of two the epilogue removes
+    constexpr int INV = FMT == TF_T4 ? 4 : FMT == TF_F4 ? 1 : 0;
     constexpr int MB = MBX > 0 ? MBX : gemv_step_blocks(FMT, NT);  // blocks per step
     constexpr int R = gemv_ring_depth(FMT, NT);  // steps per warp ring (R - 1 in flight)
     int *jp = reinterpret_cast<int *>(smem + OFF_JP);
@@ -753,7 +779,7 @@ __device__ __forceinline__ void gemv_cta(const GemvParams &p, uint8_t *smem, int
         int rows[GEMV_MAXR];
 #pragma unroll
         for (int r = 0; r < GEMV_MAXR; ++r) rows[r] = r;
-        fill_B<NT, CPB>(p, rows, p.shared_rows, meta, 0, Bsm, cw, lane, ctid);
+        fill_B<NT, CPB, INV>(p, rows, p.shared_rows, meta, 0, Bsm, cw, lane, ctid);
     }
     int jfill = -1;
     float acc[NT][4];
@@ -778,12 +804,12 @@ __device__ __forceinline__ void gemv_cta(const GemvParams &p, uint8_t *smem, int
             const int kc = kb0 + c * MB + i;
             BlkRegs r;
             load_blk_smem<FMT, GS>(r, slot + i * BB, lane);
-            if (FMT == TF_T4) {
+            if (tf_4bit(FMT)) {
                 uint4 B[NT];
 #pragma unroll
                 for (int nt = 0; nt < NT; ++nt)
                     B[nt] = reinterpret_cast<const uint4 *>(Bsm)[(nt * p.kblocks + kc) * 32 + lane];
-                block_t4<NT, GS>(r, B, acc, ia);
+                block_t4<FMT, NT, GS>(r, B, acc, ia);
             } else {
                 uint2 B[NT];
 #pragma unroll
@@ -820,7 +846,7 @@ __device__ __forceinline__ void gemv_cta(const GemvParams &p, uint8_t *smem, int
                 }
                 named_bar_sync(BAR_FILL, NCT);
             } else {
-                fill_B<NT, CPB>(p, job.in_row, job.nrows, meta, mb, Bsm, cw, lane, ctid);
+                fill_B<NT, CPB, INV>(p, job.in_row, job.nrows, meta, mb, Bsm, cw, lane, ctid);
                 jfill = j;
             }
         }

@@ -197,6 +197,11 @@ cudaError_t gen_i4_rowmajor(uint8_t *q4, float *scales, int O, int I, int gs, ui
                             float std_, cudaStream_t st);
 cudaError_t gen_i8_rowmajor(int8_t *q8, float *scales, int O, int I, uint64_t seed, float std_,
                             cudaStream_t st);
+// The same N(0, std) weights as MXFP4 (OCP rule: shared exponent
+// floor(log2 max|w|) - 2, E2M1 round-to-nearest-even, saturating), codes in
+// the packed host layout and one decoded scale per 32 columns.  I % 32 == 0.
+cudaError_t gen_f4_rowmajor(uint8_t *q4, float *scales, int O, int I, uint64_t seed, float std_,
+                            cudaStream_t st);
 cudaError_t gen_f32(float *dst, int64_t n, uint64_t seed, float mean, float std_, cudaStream_t st);
 // N(0, 1) into n elements of a KV cache (fp32 or bf16) starting at element off.
 cudaError_t gen_kv(void *base, int64_t off, int64_t n, int bf16, uint64_t seed, cudaStream_t st);

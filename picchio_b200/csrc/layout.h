@@ -16,6 +16,13 @@
 //  T8 (INT8): same 16-row tiles, blocks of 32 columns = 512 bytes, one
 //   m16n8k32 step: word 2h + r of lane 4g + t has columns 16h + 4t + j of
 //   row g (r = 0) or g + 8 (r = 1); plus a float[O] row-scale array.
+//  F4 (MXFP4, OCP microscaling: E2M1 codes with one scale per 32 columns):
+//   the T4 block geometry with group size 32, but word q of a lane holds the
+//   four 4-bit codes of row g in bits 0-15 (column 32m + 16h + 4t + j in
+//   bits 4j..4j+3) and those of row g + 8 in bits 16-31, so that one
+//   byte-permute turns 16 bits into four signed bytes (2 x the E2M1 value:
+//   0, 1, 2, 3, 4, 6, 8, 12 with the code's sign); the scales are the
+//   decoded E8M0 factors 2^(e - 127) as fp32.
 //  F32: row-major float[O][I].
 //
 // A row tile is therefore one contiguous byte range in which every lane's
@@ -32,14 +39,16 @@
 
 namespace pc {
 
-enum TileFmt { TF_F32 = 0, TF_T8 = 1, TF_T4 = 2 };
+enum TileFmt { TF_F32 = 0, TF_T8 = 1, TF_T4 = 2, TF_F4 = 3 };
+// 4-bit formats share the T4 block geometry (64 columns per block).
+__host__ __device__ constexpr bool tf_4bit(int fmt) { return fmt == TF_T4 || fmt == TF_F4; }
 enum RowPerm { PERM_NONE = 0, PERM_PAIR = 1, PERM_HEAD = 2 };
 
 struct TileDesc {
     int fmt = TF_F32;
     int O = 0, I = 0;       // logical shape
-    int Op = 0, Ip = 0;     // padded: Op % 16 == 0; Ip % 64 (T4) or % 32 (T8)
-    int gs = 0;             // T4 group size (16, 32, 64) or 0 = per-row scale
+    int Op = 0, Ip = 0;     // padded: Op % 16 == 0; Ip % 64 (T4, F4) or % 32 (T8)
+    int gs = 0;             // T4 group size (16, 32, 64) or 0 = per-row scale; F4: 32
     int kblocks = 0;        // blocks per row tile
     int blk_bytes = 0;
     int64_t unit_bytes = 0; // bytes per row tile
@@ -94,7 +103,7 @@ enum GemvEpi {
 struct GemvParams {
     const GemvJob *jobs;
     const int *njobs;       // device-resident job count
-    int fmt;                // TF_T4 / TF_T8 (must match the kernel instance)
+    int fmt;                // TF_T4 / TF_F4 / TF_T8 (must match the kernel instance)
     int gs;                 // T4 group size or 0
     int kblocks, blk_bytes;
     int I, Ip;              // input row length (logical, padded)

@@ -245,10 +245,43 @@ struct ExpertMat {
     std::vector<uint8_t> q;
     std::vector<float> s;
     int bs = 0;
+    int fmt = TF_T4;  // TF_T4 (INT4) or TF_F4 (MXFP4)
 };
+
+// Expert e of the checkpoint's own MXFP4 form (the layout convert.py:400-431
+// reads before requantizing): `<which>_blocks` U8 [E][O][I/32][16] (two E2M1
+// codes per byte, low nibble = even column) and `<which>_scales` U8
+// [E][O][I/32] (E8M0: factor 2^(e - 127)).  Kept as MXFP4 (the reference's
+// fmt 3) instead of converted to INT4.
+pc_status expert_matrix_mxfp4(const StDB &db, int layer, int eid, const char *which, int O, int I, ExpertMat &m,
+                              bool *found) {
+    char bn[300], sn[300];
+    snprintf(bn, sizeof bn, "model.layers.%d.mlp.experts.%s_blocks", layer, which);
+    snprintf(sn, sizeof sn, "model.layers.%d.mlp.experts.%s_scales", layer, which);
+    const StTensor *tb = db.find(bn), *ts = db.find(sn);
+    *found = tb && ts;
+    if (!*found) return PC_OK;
+    if (tb->dtype != ST_U8 || ts->dtype != ST_U8) return fail(PC_ERR_FORMAT, std::string(bn) + ": MXFP4 blocks and scales must be U8");
+    if (I % 32) return fail(PC_ERR_FORMAT, std::string(bn) + ": MXFP4 rows must be a multiple of 32 columns");
+    const int64_t rb = I / 2, nb = I / 32;
+    if (tb->nbytes() < (int64_t)(eid + 1) * O * rb || ts->nbytes() < (int64_t)(eid + 1) * O * nb)
+        return fail(PC_ERR_FORMAT, std::string(bn) + ": fewer experts or smaller rows than the config");
+    m.q.resize((size_t)(O * rb));
+    if (!db.read(*tb, m.q.data(), (int64_t)O * rb, (int64_t)eid * O * rb)) return fail(PC_ERR_IO, std::string("short read: ") + bn);
+    std::vector<uint8_t> e8((size_t)(O * nb));
+    if (!db.read(*ts, e8.data(), (int64_t)O * nb, (int64_t)eid * O * nb)) return fail(PC_ERR_IO, std::string("short read: ") + sn);
+    m.s.resize(e8.size());
+    for (size_t i = 0; i < e8.size(); ++i) m.s[i] = ldexpf(1.0f, (int)e8[i] - 127);  // decode_e8m0, convert.py:129-134
+    m.bs = 32;
+    m.fmt = TF_F4;
+    return PC_OK;
+}
 
 // The weight half of expert_load (picchio.c:712-866) for one matrix.
 pc_status expert_matrix(const StDB &db, int layer, int eid, const char *which, int O, int I, ExpertMat &m) {
+    bool mx = false;
+    PC_TRY(expert_matrix_mxfp4(db, layer, eid, which, O, I, m, &mx));
+    if (mx) return PC_OK;
     char nm[300];
     const char *fmts[3] = {"model.layers.%d.mlp.experts.%s.%d", "model.layers.%d.mlp.experts.%d.%s",
                            "model.layers.%d.mlp.experts.%d.%s.weight"};
@@ -277,11 +310,11 @@ pc_status expert_matrix(const StDB &db, int layer, int eid, const char *which, i
     return PC_OK;
 }
 
-pc_status expert_geometry(pc_ctx *c, int gs_gu, int gs_dn) {
+pc_status expert_geometry(pc_ctx *c, int gs_gu, int gs_dn, int fmt) {
     const pc_model_cfg &k = c->cfg;
     ExpertGeom &g = c->eg;
-    tile_geom(g.gu, TF_T4, 2 * k.intermediate, k.hidden, gs_gu, PERM_PAIR, 0);
-    tile_geom(g.dn, TF_T4, k.hidden, k.intermediate, gs_dn, PERM_NONE, 0);
+    tile_geom(g.gu, fmt, 2 * k.intermediate, k.hidden, gs_gu, PERM_PAIR, 0);
+    tile_geom(g.dn, fmt, k.hidden, k.intermediate, gs_dn, PERM_NONE, 0);
     int64_t off = 0;
     g.off_gu = off; off = align256(off + tile_bytes(g.gu));
     g.off_dn = off; off = align256(off + tile_bytes(g.dn));
@@ -370,11 +403,11 @@ void tile_geom(TileDesc &t, int fmt, int O, int I, int gs, int perm, int hd) {
     t.fmt = fmt;
     t.O = O;
     t.I = I;
-    t.gs = fmt == TF_T4 ? gs : 0;
+    t.gs = fmt == TF_T4 ? gs : fmt == TF_F4 ? 32 : 0;
     t.perm = perm;
     t.head_dim = hd;
     t.Op = round_up(O, 16);
-    if (fmt == TF_T4) {
+    if (tf_4bit(fmt)) {
         t.Ip = round_up(I, 64);
         t.kblocks = t.Ip / 64;
         t.blk_bytes = t4_blk_bytes(t.gs);
@@ -565,16 +598,18 @@ pc_status load_model(pc_ctx *c, const std::string &dir) {
             ExpertMat gu, dn;
             PC_TRY(expert_matrix(db, l, e, "gate_up_proj", I2, D, gu));
             PC_TRY(expert_matrix(db, l, e, "down_proj", D, k.intermediate, dn));
+            if (gu.fmt != dn.fmt) return fail(PC_ERR_FORMAT, "gate_up and down experts in different formats");
             if (!geom) {
-                PC_TRY(expert_geometry(c, gu.bs, dn.bs));
+                PC_TRY(expert_geometry(c, gu.bs, dn.bs, gu.fmt));
+                k.expert_format = gu.fmt == TF_F4 ? PC_FMT_MXFP4 : PC_FMT_INT4;
                 if (c->opts.expert_residency == 1) PC_TRY(res_init(c));
                 geom = true;
                 const int64_t raw = (int64_t)I2 * ((D + 1) / 2) + (int64_t)gu.s.size() * 4 +
                                     (int64_t)D * ((k.intermediate + 1) / 2) + (int64_t)dn.s.size() * 4 + 1024;
                 PC_CU(cudaMalloc(&dtmp, raw));
             }
-            if (gu.bs != c->eg.gu.gs || dn.bs != c->eg.dn.gs)
-                return fail(PC_ERR_FORMAT, "experts with different INT4 group sizes in one model");
+            if (gu.bs != c->eg.gu.gs || dn.bs != c->eg.dn.gs || gu.fmt != c->eg.gu.fmt)
+                return fail(PC_ERR_FORMAT, "experts with different formats or group sizes in one model");
             if (!c->L[l].experts)
                 PC_TRY(dalloc(c, (size_t)(c->e_hi - c->e_lo) * c->eg.stride, (void **)&c->L[l].experts));
             // streamed residency: assembled in a staging expert, then stored on the host
@@ -679,7 +714,9 @@ pc_status synth_model(pc_ctx *c, uint64_t seed) {
         PC_TRY(vec((int64_t)E * D, 0.0f, 0.1f, &ly.router));
         PC_TRY(vec(E, 0.0f, 0.01f, &ly.router_bias));
     }
-    PC_TRY(expert_geometry(c, k.group_size, k.group_size));
+    const bool f4 = k.expert_format == PC_FMT_MXFP4;
+    if (f4) k.group_size = 32;
+    PC_TRY(expert_geometry(c, k.group_size, k.group_size, f4 ? TF_F4 : TF_T4));
     if (c->opts.expert_residency == 1) PC_TRY(res_init(c));
     for (int l = 0; l < k.n_layers; ++l) {
         if (!c->res.on) PC_TRY(dalloc(c, (size_t)(c->e_hi - c->e_lo) * c->eg.stride, (void **)&c->L[l].experts));
@@ -687,9 +724,11 @@ pc_status synth_model(pc_ctx *c, uint64_t seed) {
             uint8_t *base = c->res.on ? c->res.stage : c->L[l].experts + (int64_t)(e - c->e_lo) * c->eg.stride;
             TileDesc tg, td;
             expert_views(c, base, tg, td);
-            PC_CU(gen_i4_rowmajor(tmp, tmps, I2, D, k.group_size, seed_of(seed, 1000 + l, e, 1), 0.02f, st));
+            if (f4) PC_CU(gen_f4_rowmajor(tmp, tmps, I2, D, seed_of(seed, 1000 + l, e, 1), 0.02f, st));
+            else PC_CU(gen_i4_rowmajor(tmp, tmps, I2, D, k.group_size, seed_of(seed, 1000 + l, e, 1), 0.02f, st));
             PC_CU(retile_t4(tmp, tmps, k.group_size, tg, st));
-            PC_CU(gen_i4_rowmajor(tmp, tmps, D, k.intermediate, k.group_size, seed_of(seed, 1000 + l, e, 2), 0.02f, st));
+            if (f4) PC_CU(gen_f4_rowmajor(tmp, tmps, D, k.intermediate, seed_of(seed, 1000 + l, e, 2), 0.02f, st));
+            else PC_CU(gen_i4_rowmajor(tmp, tmps, D, k.intermediate, k.group_size, seed_of(seed, 1000 + l, e, 2), 0.02f, st));
             PC_CU(retile_t4(tmp, tmps, k.group_size, td, st));
             PC_CU(gen_f32(reinterpret_cast<float *>(base + c->eg.off_gu_b), I2, seed_of(seed, 1000 + l, e, 3), 0.0f, 0.01f, st));
             PC_CU(gen_f32(reinterpret_cast<float *>(base + c->eg.off_dn_b), D, seed_of(seed, 1000 + l, e, 4), 0.0f, 0.01f, st));

@@ -916,6 +916,10 @@ pc_status tc_setup(pc_ctx *c) {
 pc_status finish_init(pc_ctx *c) {
     if (c->opts.ep_size > 1) PC_TRY(ep_init(c));
     PC_TRY(tc_setup(c));
+    // Allocations are zeroed with cudaMemset, on the legacy default stream:
+    // the context's non-blocking stream does not wait for it, so every
+    // zeroing (and upload) must be complete before the first step runs.
+    PC_CU(cudaDeviceSynchronize());
     return PC_OK;
 }
 

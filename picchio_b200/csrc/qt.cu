@@ -132,6 +132,7 @@ pc_status pc_qt_create(int device, int fmt, int O, int I, int block_size, const 
     if (fmt != PC_FMT_F32 && !scales) return fail(PC_ERR_INVALID_ARG, "quantized weights need scales");
     if (fmt == PC_FMT_INT4 && block_size != 0 && block_size != 16 && block_size != 32 && block_size != 64)
         return fail(PC_ERR_FORMAT, "INT4 block size must be 0, 16, 32 or 64");
+    if (fmt == PC_FMT_MXFP4 && block_size != 32) return fail(PC_ERR_FORMAT, "MXFP4 blocks are 32 columns");
     pc_qt *w = new pc_qt();
     w->dev = device;
     pc_status s = device_setup(device, &w->nsm, &w->max_smem);
@@ -146,9 +147,11 @@ pc_status pc_qt_create(int device, int fmt, int O, int I, int block_size, const 
             return done(fail(PC_ERR_CUDA, "upload"));
         return done(PC_OK);
     }
-    const bool i4 = fmt == PC_FMT_INT4;
+    // INT4 and MXFP4 share the host layout: two 4-bit values per byte, low
+    // nibble = even column; MXFP4 scales are one float per 32 columns
+    const bool i4 = fmt == PC_FMT_INT4 || fmt == PC_FMT_MXFP4;
     if (!i4 && fmt != PC_FMT_INT8) return done(fail(PC_ERR_FORMAT, "unknown format"));
-    tile_geom(w->t, i4 ? TF_T4 : TF_T8, O, I, i4 ? block_size : 0, PERM_NONE, 0);
+    tile_geom(w->t, fmt == PC_FMT_MXFP4 ? TF_F4 : i4 ? TF_T4 : TF_T8, O, I, i4 ? block_size : 0, PERM_NONE, 0);
     if ((s = qalloc(w, (size_t)tile_bytes(w->t), (void **)&w->t.tiles)) != PC_OK) return done(s);
     if (!i4 || block_size == 0)
         if ((s = qalloc(w, (size_t)w->t.Op * 4, (void **)&w->t.rs)) != PC_OK) return done(s);

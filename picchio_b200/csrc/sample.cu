@@ -560,6 +560,9 @@ cudaError_t sampler_init(Sampler &s, int V) {
     if (e == cudaSuccess)
         e = cub::DeviceRadixSort::SortPairsDescending(nullptr, s.tmp_bytes, s.ck, s.sk, s.cv, s.sv, V);
     if (e == cudaSuccess) e = cudaMalloc(&s.tmp, s.tmp_bytes);
+    // the memsets above run on the legacy default stream, which a
+    // context's non-blocking stream does not wait for
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
     return e;
 }
 

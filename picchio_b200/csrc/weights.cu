@@ -13,17 +13,22 @@ namespace pc {
 
 namespace {
 
-__device__ __forceinline__ int src_nibble(const uint8_t *q4, int O, int I, int row, int col) {
-    if (row >= O || col >= I) return 8;  // padding: value 0
+__device__ __forceinline__ int src_nibble(const uint8_t *q4, int O, int I, int row, int col, int pad) {
+    if (row >= O || col >= I) return pad;  // padding: value 0
     const uint8_t b = q4[(int64_t)row * ((I + 1) / 2) + (col >> 1)];
     return (col & 1) ? (b >> 4) : (b & 0xF);
 }
 
 // One thread per (row tile, block, lane): 16 bytes of nibbles (+ the scales
 // of rows g and g+8 for lanes with t == 0).  Word q = 2m + h of lane 4g + t
-// holds columns 64kc + 32m + 16h + 4t + j (j = 0..3) in byte j: row g in the
-// low nibble, row g + 8 in the high nibble.
+// holds columns 64kc + 32m + 16h + 4t + j (j = 0..3): for INT4 in byte j, row
+// g in the low nibble and row g + 8 in the high nibble; for MXFP4 (F4) row
+// g's codes in bits 4j..4j+3 and row g + 8's in bits 16 + 4j.. (the source
+// layout is the same for both: two 4-bit values per byte, low nibble = even
+// column, as quant.h:32-41 and the MXFP4 blocks of convert.py:413-420 store
+// them).  Padding is the value 0: nibble 8 for INT4, code 0 for MXFP4.
 __global__ void retile_t4_kernel(const uint8_t *q4, const float *scales, int bs, TileDesc d) {
+    const bool f4 = d.fmt == TF_F4;
     const int64_t total = (int64_t)(d.Op / 16) * d.kblocks * 32;
     const int ng = bs > 0 ? (d.I + bs - 1) / bs : 1;
     for (int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; idx < total;
@@ -38,9 +43,11 @@ __global__ void retile_t4_kernel(const uint8_t *q4, const float *scales, int bs,
         for (int q = 0; q < 4; ++q) {
             const int c = kc * 64 + 32 * (q >> 1) + 16 * (q & 1) + 4 * t;
             uint32_t v = 0;
-            for (int j = 0; j < 4; ++j)
-                v |= ((uint32_t)src_nibble(q4, d.O, d.I, rlo, c + j) << (8 * j)) |
-                     ((uint32_t)src_nibble(q4, d.O, d.I, rhi, c + j) << (8 * j + 4));
+            for (int j = 0; j < 4; ++j) {
+                const uint32_t lo = src_nibble(q4, d.O, d.I, rlo, c + j, f4 ? 0 : 8);
+                const uint32_t hi = src_nibble(q4, d.O, d.I, rhi, c + j, f4 ? 0 : 8);
+                v |= f4 ? (lo << (4 * j)) | (hi << (16 + 4 * j)) : (lo << (8 * j)) | (hi << (8 * j + 4));
+            }
             w[q] = v;
         }
         uint8_t *dst = d.tiles + blk * d.blk_bytes;
@@ -115,12 +122,18 @@ __global__ void dequant_tiles_kernel(TileDesc d, float *out) {
         logical_to_tile(d.perm, d.head_dim, lr, rt, tr);
         const int g = tr & 7, rh = tr >> 3;
         float v, s;
-        if (d.fmt == TF_T4) {
+        if (tf_4bit(d.fmt)) {
             const int kc = c / 64, r = c % 64;
             const int q = 2 * (r / 32) + (r % 32) / 16, t = (r % 16) / 4, j = r % 4;
             const uint8_t *blk = d.tiles + ((int64_t)rt * d.kblocks + kc) * d.blk_bytes;
             const uint32_t w = *reinterpret_cast<const uint32_t *>(blk + (4 * g + t) * 16 + q * 4);
-            v = (float)((int)((w >> (8 * j + 4 * rh)) & 0xF) - 8);
+            if (d.fmt == TF_F4) {  // E2M1 (convert.py:98-103): code 8 is -0
+                const int code = (int)((w >> (4 * j + 16 * rh)) & 0xF);
+                const float mag[8] = {0.0f, 0.5f, 1.0f, 1.5f, 2.0f, 3.0f, 4.0f, 6.0f};
+                v = (code & 8) ? -mag[code & 7] : mag[code & 7];
+            } else {
+                v = (float)((int)((w >> (8 * j + 4 * rh)) & 0xF) - 8);
+            }
             if (d.gs > 0) {
                 const int gpc = 64 / d.gs, jg = r / d.gs;
                 s = reinterpret_cast<const float *>(blk + 512)[g * gpc * 2 + jg * 2 + rh];
@@ -176,6 +189,43 @@ __global__ void gen_i4_kernel(uint8_t *q4, float *scales, int O, int I, int gs, 
                 v1 = max(-8, min(7, v1));
             }
             q4[(int64_t)row * rb + (c >> 1)] = (uint8_t)((v0 + 8) | ((v1 + 8) << 4));
+        }
+    }
+}
+
+// MXFP4 per the OCP microscaling rule, one thread per 32-column block: the
+// shared exponent is floor(log2(max |w|)) - 2 (2 = the largest E2M1
+// exponent), clamped to [-127, 127], stored as the E8M0 byte + 127; each
+// w / 2^exp rounds to the nearest E2M1 value (0, 0.5, 1, 1.5, 2, 3, 4, 6;
+// ties to the even code; beyond 6 saturates), sign in bit 3.  The decoded
+// scale 2^exp goes to `scales` as a float.
+__device__ __forceinline__ int e2m1_code(float v) {
+    const float a = fabsf(v);
+    const float mids[7] = {0.25f, 0.75f, 1.25f, 1.75f, 2.5f, 3.5f, 5.0f};
+    int idx = 0;
+    for (int i = 0; i < 7; ++i) idx += mids[i] < a;
+    if (idx < 7 && a == mids[idx] && (idx & 1)) ++idx;  // tie: the even code
+    return idx | (v < 0.0f ? 8 : 0);
+}
+
+__global__ void gen_f4_kernel(uint8_t *q4, float *scales, int O, int I, uint64_t seed, float sd) {
+    const int nb = I / 32;
+    const int64_t total = (int64_t)O * nb;
+    for (int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; idx < total;
+         idx += (int64_t)gridDim.x * blockDim.x) {
+        const int row = (int)(idx / nb), b = (int)(idx % nb);
+        float w[32], amax = 0.0f;
+        for (int j = 0; j < 32; ++j) {
+            w[j] = __fmul_rn(normal_at(seed, (uint64_t)row * I + b * 32 + j), sd);
+            amax = fmaxf(amax, fabsf(w[j]));
+        }
+        int ex = amax > 0.0f ? (int)((__float_as_uint(amax) >> 23) & 0xFF) - 127 - 2 : -127;
+        ex = max(-127, min(127, ex));
+        const float inv = ldexpf(1.0f, -ex), sc = ldexpf(1.0f, ex);
+        scales[idx] = sc;
+        for (int j = 0; j < 32; j += 2) {
+            const int c0 = e2m1_code(__fmul_rn(w[j], inv)), c1 = e2m1_code(__fmul_rn(w[j + 1], inv));
+            q4[(int64_t)row * (I / 2) + b * 16 + j / 2] = (uint8_t)(c0 | (c1 << 4));
         }
     }
 }
@@ -239,6 +289,12 @@ cudaError_t gen_i4_rowmajor(uint8_t *q4, float *scales, int O, int I, int gs, ui
                             cudaStream_t st) {
     const int ng = gs > 0 ? (I + gs - 1) / gs : 1;
     gen_i4_kernel<<<grid_for((int64_t)O * ng, 128), 128, 0, st>>>(q4, scales, O, I, gs, seed, sd);
+    return cudaGetLastError();
+}
+
+cudaError_t gen_f4_rowmajor(uint8_t *q4, float *scales, int O, int I, uint64_t seed, float sd, cudaStream_t st) {
+    if (I % 32) return cudaErrorInvalidValue;
+    gen_f4_kernel<<<grid_for((int64_t)O * (I / 32), 128), 128, 0, st>>>(q4, scales, O, I, seed, sd);
     return cudaGetLastError();
 }
 

@@ -14,7 +14,10 @@ discovery, picchio.c:2385-2650 dense tensors, picchio.c:698-888 experts):
   ``mlp.router.bias`` F32 [E]; ``mlp.experts.gate_up_proj_bias`` F32 [E, I2];
   ``mlp.experts.down_proj_bias`` F32 [E, D];
   per expert ``mlp.experts.gate_up_proj.E`` / ``mlp.experts.down_proj.E``
-  U8 packed INT4 + ``.qs`` F32 group scales.
+  U8 packed INT4 + ``.qs`` F32 group scales; or, with ``expert_format =
+  "mxfp4"``, the checkpoint's own MXFP4 form instead:
+  ``mlp.experts.gate_up_proj_blocks`` U8 [E, I2, D/32, 16] with
+  ``..._scales`` U8 [E, I2, D/32] (E8M0), and the same for ``down_proj``.
 
 Quantizers follow the reference converter (convert.py:45-93 INT4: amax/7
 with a 1e-8 floor, round half to even, clip [-8, 7], low nibble = even
@@ -55,13 +58,14 @@ class SynthConfig:
     layer_types: list = field(default_factory=lambda: ["sliding_attention", "full_attention"])
     # container options (not written to config.json)
     group_size: int = 32          # expert INT4 group size; 0 = per-row scale
+    expert_format: str = "int4"   # "int4" | "mxfp4" (the checkpoint's own _blocks/_scales form)
     attn_format: str = "i8"       # "i8" | "f32" | "i4"
     attn_group_size: int = 0      # for attn_format == "i4"
     rope_scaling: dict | None = None  # e.g. {"rope_type": "yarn", "factor": 32.0, ...}
 
     def config_json(self) -> dict:
         d = {k: v for k, v in asdict(self).items()
-             if k not in ("group_size", "attn_format", "attn_group_size", "rope_scaling")}
+             if k not in ("group_size", "attn_format", "attn_group_size", "rope_scaling", "expert_format")}
         d["model_type"] = "gpt_oss"
         d["attention_bias"] = True
         if self.rope_scaling:
@@ -105,6 +109,34 @@ def quantize_int4(w: np.ndarray, group_size: int):
     if I % 2:
         packed[:, -1] &= 0xF
     return packed.astype(np.uint8), scales
+
+
+E2M1_MIDS = np.array([0.25, 0.75, 1.25, 1.75, 2.5, 3.5, 5.0], np.float32)
+
+
+def quantize_mxfp4(w: np.ndarray):
+    """MXFP4 by the OCP microscaling rule, per 32-column block: shared
+    exponent floor(log2 max|w|) - 2 (2 = the largest E2M1 exponent), clamped
+    to [-127, 127] and stored as the E8M0 byte exp + 127; each w / 2^exp
+    rounds to the nearest E2M1 value (0, 0.5, 1, 1.5, 2, 3, 4, 6; ties to the
+    even code; saturating at 6), sign in bit 3.  Returns (blocks uint8 [O,
+    I/32, 16], two codes per byte with the low nibble the even column, and
+    scales uint8 [O, I/32]): the checkpoint layout convert.py:400-431 reads."""
+    O, I = w.shape
+    assert I % 32 == 0
+    b = w.astype(np.float32).reshape(O, I // 32, 32)
+    amax = np.abs(b).max(-1)
+    bits = amax.view(np.uint32)
+    ex = np.where(amax > 0, ((bits >> 23) & 0xFF).astype(np.int32) - 127 - 2, -127)
+    ex = np.clip(ex, -127, 127)
+    v = (b * np.ldexp(np.float32(1), -ex)[..., None].astype(np.float32)).astype(np.float32)
+    a = np.abs(v)
+    idx = np.searchsorted(E2M1_MIDS, a, side="left")  # mids strictly below a
+    tie = (idx < 7) & (a == E2M1_MIDS[np.minimum(idx, 6)]) & ((idx & 1) == 1)
+    idx = idx + tie
+    code = (idx | np.where(v < 0, 8, 0)).astype(np.uint8).reshape(O, I)
+    packed = (code[:, 0::2] | (code[:, 1::2] << 4)).astype(np.uint8).reshape(O, I // 32, 16)
+    return packed, (ex + 127).astype(np.uint8)
 
 
 def quantize_int8(w: np.ndarray):
@@ -197,6 +229,22 @@ def make_model(out_dir: str, cfg: SynthConfig = TINY, seed: int = 1234) -> dict:
         t[p + "mlp.router.bias"] = normal((E,), 0.01)
         t[p + "mlp.experts.gate_up_proj_bias"] = normal((E, I2), 0.01)
         t[p + "mlp.experts.down_proj_bias"] = normal((E, D), 0.01)
+        if cfg.expert_format == "mxfp4":
+            # one aggregated tensor per projection, [E][rows][I/32][16] codes
+            # and [E][rows][I/32] E8M0 scales
+            gub, gus, dnb, dns = [], [], [], []
+            for e in range(E):
+                b_, s_ = quantize_mxfp4(normal((I2, D), 0.02))
+                gub.append(b_)
+                gus.append(s_)
+                b_, s_ = quantize_mxfp4(normal((D, Iin), 0.02))
+                dnb.append(b_)
+                dns.append(s_)
+            t[p + "mlp.experts.gate_up_proj_blocks"] = np.stack(gub)
+            t[p + "mlp.experts.gate_up_proj_scales"] = np.stack(gus)
+            t[p + "mlp.experts.down_proj_blocks"] = np.stack(dnb)
+            t[p + "mlp.experts.down_proj_scales"] = np.stack(dns)
+            continue
         # draws stay in order on this thread; the quantization of each
         # matrix runs on a worker while the next one is drawn
         # (at most LAG experts in flight, which bounds the float copies held)

@@ -10,12 +10,17 @@ containers written by ``picchio_b200.synth`` and records:
 * ``<name>_dumps.npz``: the reference's ``ORACLE_DIR`` stage dumps of its last
   forward (picchio.c:204-249), used as per-layer parity probes;
 * ``kernels.npz``: reference ``matmul_qt`` outputs (quant.h:117-319) on seeded
-  small inputs, via ``oracle/_ref/libpicchio_ref.so``.
+  small inputs, via ``oracle/_ref/libpicchio_ref.so``;
+* ``mxfp4.npz``: MXFP4 blocks / E8M0 scales (every code and a spread of
+  exponents) and their fp32 values from the reference converter's own
+  ``dequant_mxfp4_fast`` / ``dequant_mxfp4`` and ``decode_e8m0``
+  (convert.py:129-213), imported from the reference sources.
 
 Needs the reference sources (``REF=...``, else BASELINE.json's
 ``reference_path``) only to build ``oracle/_ref``; the
 fixtures it writes are small and committed, and the tests read only them.
-Usage: ``python tests/golden/make_golden.py [tiny] [gptoss] [service]`` (all by default).
+Usage: ``python tests/golden/make_golden.py [tiny] [gptoss] [gptoss_bf16kv] [service] [mxfp4]`` (all by
+default).
 """
 from __future__ import annotations
 
@@ -224,9 +229,10 @@ def make_gptoss_bf16kv():
     a bf16 KV cache (OracleModel(kv_bf16=True): every stored K/V row rounded
     to bf16, the device's cache format; the rest is the oracle restatement
     pinned bit-exact to the reference).  Teacher-forced on the reference's
-    ids, as the device test runs; the GPTOSS_PROBE_KEYS stage tensors at the
-    probe calls, every stage tensor of the last call, and of the last call
-    after the long prompt."""
+    ids, as the device test runs; the greedy next id and router top-k of
+    every call, the GPTOSS_PROBE_KEYS stage tensors at the probe calls, every
+    stage tensor of the last call, and of the last call after the long
+    prompt."""
     with open(os.path.join(HERE, "gptoss_2l.json")) as f:
         meta = json.load(f)
     cfg = SynthConfig(**GPTOSS)
@@ -235,10 +241,13 @@ def make_gptoss_bf16kv():
         make_model(d, cfg, GPTOSS_SEED)
         m = O.OracleModel(d, ctx=meta["ctx"], kv_bf16=True)
         prompt, ids = meta["prompt"], meta["ids"]
+        nxt, topk = [], []
         for i, t in enumerate(prompt):
-            m.forward_token(t, i)
+            first = m.forward_token(t, i)
+        nxt.append(first)
         for s in range(1, GPTOSS_STEPS + 1):
-            m.forward_token(ids[s - 1], len(prompt) + s - 1)
+            nxt.append(m.forward_token(ids[s - 1], len(prompt) + s - 1))
+            topk.append(np.stack([m.dumps[f"layer{l}.top_indices"].reshape(-1) for l in range(2)]))
             if s in GPTOSS_PROBES:
                 for k in GPTOSS_PROBE_KEYS:
                     arrays[f"probe{s}.{k}"] = m.dumps[k].reshape(-1).astype(np.float32)
@@ -246,6 +255,8 @@ def make_gptoss_bf16kv():
                 for k, v in m.dumps.items():
                     if STAGE_RE.match(k):
                         arrays[f"last.{k}"] = np.asarray(v).reshape(-1).astype(np.float32)
+        arrays["next_ids"] = np.array(nxt, np.int32)          # after the prompt, then after each call
+        arrays["top_indices"] = np.stack(topk).astype(np.int32)  # [call][layer][k]
         m = O.OracleModel(d, ctx=meta["ctx"], kv_bf16=True)
         lp, lids = meta["long_prompt"], meta["long_ids"]
         for i, t in enumerate(lp):
@@ -306,9 +317,37 @@ def make_service():
     print("service transcript:", svc.count("\n"), "lines;", "ids run:", ids_out.split()[:8])
 
 
+def make_mxfp4():
+    """mxfp4.npz: the reference converter's MXFP4 dequantization on seeded
+    inputs.  Shapes (rows, columns): a GPT-OSS gate_up row block and two
+    small ones; codes uniform over all 16 (so -0 and +-6 occur), E8M0 bytes
+    over [100, 140] plus the extremes 0 and 254 in the small case."""
+    src = O.reference_dir()
+    if not src:
+        raise SystemExit("set REF=<reference checkout> (convert.py is imported from it)")
+    sys.path.insert(0, src)
+    import convert  # the reference converter (needs numpy only for these functions)
+    rng = np.random.default_rng(4)
+    out = {}
+    for tag, (rows, cols) in {"a": (64, 2880), "b": (16, 64), "c": (8, 96)}.items():
+        nb = cols // 32
+        blocks = rng.integers(0, 256, size=(rows, nb, 16), dtype=np.uint8)
+        e8 = rng.integers(100, 141, size=(rows, nb), dtype=np.uint8)
+        if tag == "b":
+            e8[0, 0], e8[1, 1] = 0, 254
+        sc = convert.decode_e8m0(e8.reshape(-1))
+        fast = convert.dequant_mxfp4_fast(blocks.reshape(-1), sc, (rows, cols), 32)
+        if tag != "a":
+            slow = convert.dequant_mxfp4(blocks.reshape(-1), sc, (rows, cols), 32)
+            assert np.array_equal(fast.view(np.uint32), slow.view(np.uint32)), tag
+        out.update({f"{tag}_blocks": blocks, f"{tag}_e8m0": e8, f"{tag}_values": fast.astype(np.float32)})
+    np.savez_compressed(os.path.join(HERE, "mxfp4.npz"), **out)
+    print("mxfp4.npz", len(out), "arrays")
+
+
 if __name__ == "__main__":
     O.build(ref=True)
-    which = sys.argv[1:] or ["tiny", "gptoss", "service"]
+    which = sys.argv[1:] or ["tiny", "gptoss", "service", "mxfp4"]
     if "tiny" in which:
         for n, o in VARIANTS.items():
             make_variant(n, o)
@@ -320,3 +359,5 @@ if __name__ == "__main__":
         make_gptoss_bf16kv()
     if "service" in which:
         make_service()
+    if "mxfp4" in which:
+        make_mxfp4()

@@ -34,6 +34,20 @@ def test_library_builds_and_exports_every_declared_symbol():
         assert hasattr(L, n)
 
 
+def test_struct_layouts_match_the_header(tmp_path):
+    """The ctypes mirrors of pc_opts, pc_model_cfg and pc_sampling have the
+    sizes a C compiler gives the header's structs (a field added on one side
+    only would make the library write past the Python struct)."""
+    from picchio_b200.api import _Cfg, _Opts, _Sampling
+    src = tmp_path / "sz.c"
+    src.write_text('#include <stdio.h>\n#include "picchio_b200.h"\nint main(void) { printf("%zu %zu %zu\\n", '
+                   "sizeof(pc_opts), sizeof(pc_model_cfg), sizeof(pc_sampling)); return 0; }\n")
+    exe = tmp_path / "sz"
+    subprocess.run(["gcc", "-I" + os.path.join(ROOT, "include"), str(src), "-o", str(exe)], check=True)
+    sizes = [int(v) for v in subprocess.run([str(exe)], capture_output=True, text=True, check=True).stdout.split()]
+    assert sizes == [C.sizeof(_Opts), C.sizeof(_Cfg), C.sizeof(_Sampling)]
+
+
 def test_status_strings_and_defaults_without_gpu():
     from picchio_b200.api import lib, _Opts
     L = lib()

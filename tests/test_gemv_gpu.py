@@ -12,7 +12,7 @@ import numpy as np
 import pytest
 
 from oracle import oracle as O
-from picchio_b200.synth import quantize_int4, quantize_int8
+from picchio_b200.synth import quantize_int4, quantize_int8, quantize_mxfp4
 
 GOLD = os.path.join(os.path.dirname(__file__), "golden")
 REL_L2 = 2e-6
@@ -70,6 +70,44 @@ def test_int8_dequant_bit_exact_and_matmul(shape):
         yr = O.matmul_q8(x, q8, s8, Oo, I)
         for s in range(S):
             assert rel_l2(y[s], yr[s]) < REL_L2
+
+
+@pytest.mark.parametrize("shape", [(64, 256), (5760, 2880), (2880, 2880), (33, 96), (17, 160)])
+def test_mxfp4_dequant_bit_exact_and_matmul(shape):
+    """The reference's fmt 3 (MXFP4) natively: dequantized values bit-equal
+    to convert.py's FP4_LUT[code] * 2^(e - 127) (-0.0 included), products
+    against the reference's fp32 matmul (matmul_f32) of those values."""
+    import torch
+    from picchio_b200 import QT, FMT_MXFP4
+    Oo, I = shape
+    rng = np.random.default_rng(Oo * 13 + I)
+    w = (rng.standard_normal((Oo, I)) * 0.02).astype(np.float32)
+    blk, e8 = quantize_mxfp4(w)
+    pk = blk.reshape(Oo, I // 2)
+    sc = np.ldexp(np.ones((Oo, I // 32), np.float32), e8.astype(np.int32) - 127).astype(np.float32)
+    q = QT(FMT_MXFP4, Oo, I, pk, sc, block_size=32)
+    ref = O.dequant_mxfp4(pk, e8, Oo, I)
+    assert np.array_equal(bits(q.dequant().cpu().numpy()), bits(ref))
+    for S in (1, 3, 4, 5, 8, 13):
+        x = rng.standard_normal((S, I)).astype(np.float32)
+        y = q.matmul(torch.from_numpy(x).cuda()).cpu().numpy()
+        yr = O.matmul_f32(x, ref, Oo, I)
+        for s in range(S):
+            assert rel_l2(y[s], yr[s]) < REL_L2, (S, s, rel_l2(y[s], yr[s]))
+
+
+def test_mxfp4_dequant_matches_reference_converter():
+    """Device MXFP4 tiles dequantize to exactly the values the reference
+    converter's own code computes (tests/golden/mxfp4.npz, from
+    convert.py:129-213): every code, E8M0 bytes 0..254."""
+    from picchio_b200 import QT, FMT_MXFP4
+    g = np.load(os.path.join(GOLD, "mxfp4.npz"))
+    for tag in "abc":
+        blocks, e8, want = g[f"{tag}_blocks"], g[f"{tag}_e8m0"], g[f"{tag}_values"]
+        rows, cols = want.shape
+        sc = np.ldexp(np.ones(e8.shape, np.float32), e8.astype(np.int32) - 127).astype(np.float32)
+        q = QT(FMT_MXFP4, rows, cols, blocks.reshape(rows, -1), sc, block_size=32)
+        assert np.array_equal(bits(q.dequant().cpu().numpy()), bits(want)), tag
 
 
 def test_f32_matmul():

@@ -503,3 +503,23 @@ def test_tensor_core_attention_one_row_matches_one_row_kernel(monkeypatch):
             out[tc] = (t, t2, m.logits(0))
     assert out["0"][:2] == out["1"][:2]
     assert rel_l2(out["1"][2], out["0"][2]) < 1e-4
+
+
+@pytest.mark.parametrize("kv_bf16", [False, True], ids=["fp32_kv", "bf16_kv"])
+def test_mxfp4_experts_match_oracle(tmp_path, kv_bf16):
+    """Experts kept in the checkpoint's MXFP4 form (``<proj>_blocks`` /
+    ``_scales``, the reference's fmt 3, which its converter turns into INT4):
+    greedy ids of prefill + decode equal to the oracle's, which applies the
+    reference's fp32 matmul to convert.py's dequantized values; with a bf16
+    KV cache against the oracle with the same cache rounding."""
+    from oracle import oracle as O
+    from picchio_b200 import FMT_MXFP4, Model
+    from picchio_b200.synth import SynthConfig, make_model, random_prompt
+    d = str(tmp_path)
+    make_model(d, SynthConfig(expert_format="mxfp4"), seed=77)
+    prompt = random_prompt(40, 1024, seed=5)
+    want = O.OracleModel(d, ctx=256, kv_bf16=kv_bf16).generate(prompt, 24)
+    with Model(d, ctx=256, kv_bf16=kv_bf16) as m:
+        assert m.config["expert_format"] == FMT_MXFP4
+        got = m.generate(prompt, 24)
+    assert got == want

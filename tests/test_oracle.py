@@ -181,3 +181,17 @@ def test_sampler_restatement_matches_reference(V, setting):
         assert a == b
         assert np.array_equal(la.view(np.uint32), lb.view(np.uint32))
         assert so.rng == sr.rng and so.history == sr.history
+
+
+def test_mxfp4_dequant_matches_reference_converter():
+    """oracle.dequant_mxfp4 (the MXFP4 semantics the device follows) is
+    bit-identical to the reference converter's own dequant_mxfp4_fast /
+    decode_e8m0 (convert.py:129-213) on the committed vectors: all 16 codes
+    (-0 included) and E8M0 bytes from 0 to 254."""
+    g = np.load(os.path.join(GOLD, "mxfp4.npz"))
+    for tag in "abc":
+        blocks, e8, want = g[f"{tag}_blocks"], g[f"{tag}_e8m0"], g[f"{tag}_values"]
+        rows, cols = want.shape
+        with np.errstate(over="ignore"):
+            got = O.dequant_mxfp4(blocks.reshape(rows, -1), e8, rows, cols)
+        assert np.array_equal(got.view(np.uint32), want.view(np.uint32)), tag
