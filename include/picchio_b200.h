@@ -282,6 +282,12 @@ pc_status pc_qt_matmul(pc_qt *w, const float *x_dev, float *y_dev, int S, void *
  * the reference. */
 #define PC_QT_NOALLOC_MAX_ROWS 64
 pc_status pc_qt_matmul_noalloc(pc_qt *w, const float *x_dev, float *y_dev, int S, void *stream);
+/* Waits for `stream`, then reports (PC_ERR_TIMEOUT) and clears a device-side
+ * failure of earlier pc_qt_matmul calls on w, or of pc_qt_matmul_noalloc
+ * calls on w's device: the GEMV's bounded wait for its weight copies giving
+ * up.  Allocates nothing.  No counterpart in the reference (its matmul_qt
+ * runs on the host and cannot fail this way). */
+pc_status pc_qt_check(pc_qt *w, void *stream);
 /* out_dev[O][I] = dequantized weights, (nibble-8)*scale in fp32. */
 pc_status pc_qt_dequant(pc_qt *w, float *out_dev, void *stream);
 void pc_qt_free(pc_qt *w);

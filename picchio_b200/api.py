@@ -143,6 +143,7 @@ def lib():
         L.pc_qt_matmul.argtypes = [vp, vp, vp, C.c_int, vp]
         L.pc_qt_matmul_noalloc.argtypes = [vp, vp, vp, C.c_int, vp]
         L.pc_qt_dequant.argtypes = [vp, vp, vp]
+        L.pc_qt_check.argtypes = [vp, vp]
         L.pc_qt_free.argtypes = [vp]
         L.pc_qt_free.restype = None
         L.pc_nccl_unique_id.argtypes = [vp]
@@ -174,7 +175,7 @@ def lib():
                      "pc_decode_batch", "pc_get_logits", "pc_moe_layer", "pc_moe_experts", "pc_set_trace",
                      "pc_get_routing",
                      "pc_get_stage", "pc_dump", "pc_expert_prefetch", "pc_qt_create", "pc_qt_matmul", "pc_qt_matmul_noalloc",
-                     "pc_qt_dequant", "pc_nccl_unique_id", "pc_check_device"):
+                     "pc_qt_dequant", "pc_qt_check", "pc_nccl_unique_id", "pc_check_device"):
             getattr(L, name).restype = st
         _lib = L
     return _lib
@@ -451,6 +452,14 @@ class QT:
         st = stream if stream is not None else torch.cuda.current_stream(x.device).cuda_stream
         _check(lib().pc_qt_matmul_noalloc(self._h, _dev_ptr(x), _dev_ptr(y), x.shape[0], C.c_void_p(st)))
         return y
+
+    def check(self, stream=None):
+        """pc_qt_check: waits for the stream and raises if an earlier product
+        on this weight (or a no-alloc product on its device) reported a
+        device-side failure."""
+        import torch
+        st = stream if stream is not None else torch.cuda.current_stream(self.device).cuda_stream
+        _check(lib().pc_qt_check(self._h, C.c_void_p(st)))
 
     def dequant(self):
         import torch

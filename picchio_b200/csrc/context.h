@@ -157,6 +157,11 @@ namespace pc {
 pc_status fail(pc_status s, const std::string &msg);
 pc_status cuda_fail(cudaError_t e, const char *what);
 pc_status dalloc(pc_ctx *c, size_t bytes, void **out);
+// Host -> device copy on the context's stream, complete on return.  (A
+// plain cudaMemcpy from pageable memory returns once the data is staged,
+// with the transfer still in flight on the legacy default stream, which a
+// kernel on the context's non-blocking stream does not wait for.)
+pc_status upload(pc_ctx *c, void *dst, const void *src, size_t bytes);
 void tile_geom(TileDesc &t, int fmt, int O, int I, int gs, int perm, int hd);
 int64_t tile_bytes(const TileDesc &t);
 pc_status load_model(pc_ctx *c, const std::string &dir);

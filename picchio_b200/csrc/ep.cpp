@@ -61,7 +61,7 @@ pc_status allgather_host(pc_ctx *c, const void *mine, size_t bytes, std::vector<
     char *d = nullptr;
     PC_CU(cudaMalloc(&d, bytes * (n + 1)));
     pc_status s = PC_OK;
-    cudaError_t e = cudaMemcpy(d + bytes * n, mine, bytes, cudaMemcpyHostToDevice);
+    cudaError_t e = cudaMemcpyAsync(d + bytes * n, mine, bytes, cudaMemcpyHostToDevice, c->st);
     if (e != cudaSuccess) s = cuda_fail(e, "cudaMemcpy");
     if (s == PC_OK) {
         ncclResult_t r = api().allgather(d + bytes * n, d, bytes, ncclUint8, (ncclComm_t)c->nccl_comm, c->st);

@@ -165,7 +165,7 @@ pc_status load_dense(pc_ctx *c, const StDB &db, const std::string &name, int O, 
     if (st->dtype == ST_F32) {  // kept F32 (picchio.c:2513-2517)
         tile_geom(t, TF_F32, O, I, 0, PERM_NONE, hd);
         PC_TRY(alloc_tiles(c, t));
-        PC_CU(cudaMemcpy(t.f32, f.data(), (size_t)O * I * 4, cudaMemcpyHostToDevice));
+        PC_TRY(upload(c, t.f32, f.data(), (size_t)O * I * 4));
         return PC_OK;
     }
     // BF16 / F16 -> per-row INT4 (picchio.c:2519-2526)
@@ -190,7 +190,7 @@ pc_status load_vec(pc_ctx *c, const StDB &db, const std::string &name, int64_t n
         v.assign(n, fill);
     }
     PC_TRY(dalloc(c, (size_t)n * 4, (void **)dev));
-    PC_CU(cudaMemcpy(*dev, v.data(), (size_t)n * 4, cudaMemcpyHostToDevice));
+    PC_TRY(upload(c, *dev, v.data(), (size_t)n * 4));
     return PC_OK;
 }
 
@@ -391,8 +391,8 @@ pc_status rope_tables(pc_ctx *c) {
         }
     PC_TRY(dalloc(c, cs.size() * 4, (void **)&c->rope_cs));
     PC_TRY(dalloc(c, sn.size() * 4, (void **)&c->rope_sn));
-    PC_CU(cudaMemcpy(c->rope_cs, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice));
-    PC_CU(cudaMemcpy(c->rope_sn, sn.data(), sn.size() * 4, cudaMemcpyHostToDevice));
+    PC_TRY(upload(c, c->rope_cs, cs.data(), cs.size() * 4));
+    PC_TRY(upload(c, c->rope_sn, sn.data(), sn.size() * 4));
     return PC_OK;
 }
 
@@ -453,7 +453,7 @@ pc_status alloc_runtime(pc_ctx *c) {
     PC_TRY(dalloc(c, M * 4, (void **)&c->d_seq_one));
     std::vector<int> rows(M);
     for (int i = 0; i < M; ++i) rows[i] = i < c->nseq ? i : 0;
-    PC_CU(cudaMemcpy(c->d_seq_rows, rows.data(), M * 4, cudaMemcpyHostToDevice));
+    PC_TRY(upload(c, c->d_seq_rows, rows.data(), M * 4));
     PC_TRY(dalloc(c, (size_t)M * D * 4, (void **)&c->h));
     PC_TRY(dalloc(c, (size_t)M * D * 4, (void **)&c->hn));
     PC_TRY(dalloc(c, (size_t)M * D * 4, (void **)&c->tmp));
@@ -517,8 +517,8 @@ pc_status load_model(pc_ctx *c, const std::string &dir) {
             c->emb_fmt = TF_T8;
             PC_TRY(dalloc(c, q.size(), &c->emb));
             PC_TRY(dalloc(c, s.size() * 4, (void **)&c->emb_s));
-            PC_CU(cudaMemcpy(c->emb, q.data(), q.size(), cudaMemcpyHostToDevice));
-            PC_CU(cudaMemcpy(c->emb_s, s.data(), s.size() * 4, cudaMemcpyHostToDevice));
+            PC_TRY(upload(c, c->emb, q.data(), q.size()));
+            PC_TRY(upload(c, c->emb_s, s.data(), s.size() * 4));
         } else if (t->dtype == ST_U8) {
             const int64_t rb = (D + 1) / 2;
             std::vector<uint8_t> q((size_t)(k.vocab * rb));
@@ -539,15 +539,15 @@ pc_status load_model(pc_ctx *c, const std::string &dir) {
             c->emb_gs = bs;
             PC_TRY(dalloc(c, q.size(), &c->emb));
             PC_TRY(dalloc(c, s.size() * 4, (void **)&c->emb_s));
-            PC_CU(cudaMemcpy(c->emb, q.data(), q.size(), cudaMemcpyHostToDevice));
-            PC_CU(cudaMemcpy(c->emb_s, s.data(), s.size() * 4, cudaMemcpyHostToDevice));
+            PC_TRY(upload(c, c->emb, q.data(), q.size()));
+            PC_TRY(upload(c, c->emb_s, s.data(), s.size() * 4));
         } else {
             std::vector<float> f;
             if (!read_as_f32(db, *t, f)) return fail(PC_ERR_FORMAT, nm + ": unsupported dtype");
             if (t->dtype == ST_F32) {
                 c->emb_fmt = TF_F32;
                 PC_TRY(dalloc(c, f.size() * 4, &c->emb));
-                PC_CU(cudaMemcpy(c->emb, f.data(), f.size() * 4, cudaMemcpyHostToDevice));
+                PC_TRY(upload(c, c->emb, f.data(), f.size() * 4));
             } else {
                 std::vector<uint8_t> q((size_t)k.vocab * ((D + 1) / 2));
                 std::vector<float> s(k.vocab);
@@ -556,8 +556,8 @@ pc_status load_model(pc_ctx *c, const std::string &dir) {
                 c->emb_gs = 0;
                 PC_TRY(dalloc(c, q.size(), &c->emb));
                 PC_TRY(dalloc(c, s.size() * 4, (void **)&c->emb_s));
-                PC_CU(cudaMemcpy(c->emb, q.data(), q.size(), cudaMemcpyHostToDevice));
-                PC_CU(cudaMemcpy(c->emb_s, s.data(), s.size() * 4, cudaMemcpyHostToDevice));
+                PC_TRY(upload(c, c->emb, q.data(), q.size()));
+                PC_TRY(upload(c, c->emb_s, s.data(), s.size() * 4));
             }
         }
     }
@@ -618,20 +618,20 @@ pc_status load_model(pc_ctx *c, const std::string &dir) {
             expert_views(c, base, tg, td);
             uint8_t *d = (uint8_t *)dtmp;
             const int64_t a = (int64_t)gu.q.size(), b = (int64_t)gu.s.size() * 4, cc = (int64_t)dn.q.size();
-            PC_CU(cudaMemcpy(d, gu.q.data(), a, cudaMemcpyHostToDevice));
-            PC_CU(cudaMemcpy(d + align256(a), gu.s.data(), b, cudaMemcpyHostToDevice));
+            PC_TRY(upload(c, d, gu.q.data(), a));
+            PC_TRY(upload(c, d + align256(a), gu.s.data(), b));
             PC_CU(retile_t4(d, (const float *)(d + align256(a)), gu.bs, tg, c->st));
             PC_CU(cudaStreamSynchronize(c->st));
-            PC_CU(cudaMemcpy(d, dn.q.data(), cc, cudaMemcpyHostToDevice));
-            PC_CU(cudaMemcpy(d + align256(cc), dn.s.data(), dn.s.size() * 4, cudaMemcpyHostToDevice));
+            PC_TRY(upload(c, d, dn.q.data(), cc));
+            PC_TRY(upload(c, d + align256(cc), dn.s.data(), dn.s.size() * 4));
             PC_CU(retile_t4(d, (const float *)(d + align256(cc)), dn.bs, td, c->st));
             PC_CU(cudaStreamSynchronize(c->st));
             std::vector<float> bgu, bdn;
             bool has;
             PC_TRY(expert_bias(db, l, e, "gate_up_proj_bias", E, I2, bgu, &has));
             PC_TRY(expert_bias(db, l, e, "down_proj_bias", E, D, bdn, &has));
-            PC_CU(cudaMemcpy(base + c->eg.off_gu_b, bgu.data(), bgu.size() * 4, cudaMemcpyHostToDevice));
-            PC_CU(cudaMemcpy(base + c->eg.off_dn_b, bdn.data(), bdn.size() * 4, cudaMemcpyHostToDevice));
+            PC_TRY(upload(c, base + c->eg.off_gu_b, bgu.data(), bgu.size() * 4));
+            PC_TRY(upload(c, base + c->eg.off_dn_b, bdn.data(), bdn.size() * 4));
             if (c->res.on) PC_TRY(res_store(c, l, e));
         }
     }

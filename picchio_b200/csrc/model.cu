@@ -65,9 +65,22 @@ pc_status dalloc(pc_ctx *c, size_t bytes, void **out) {
     if (bytes == 0) bytes = 16;
     cudaError_t e = cudaMalloc(out, bytes);
     if (e != cudaSuccess) return fail(PC_ERR_OOM, "cudaMalloc(" + std::to_string(bytes) + "): " + cudaGetErrorString(e));
-    e = cudaMemset(*out, 0, bytes);
+    // Zeroed on the context's stream and waited for: a plain cudaMemset runs
+    // on the legacy default stream, which the context's non-blocking stream
+    // does not wait for, so an upload or kernel on that stream could land
+    // before the zeroing and be wiped by it.
+    e = cudaMemsetAsync(*out, 0, bytes, c->st);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(c->st);
     if (e != cudaSuccess) return cuda_fail(e, "cudaMemset");
     c->allocs.push_back(*out);
+    return PC_OK;
+}
+
+pc_status upload(pc_ctx *c, void *dst, const void *src, size_t bytes) {
+    if (bytes == 0) return PC_OK;
+    cudaError_t e = cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, c->st);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(c->st);
+    if (e != cudaSuccess) return cuda_fail(e, "host-to-device copy");
     return PC_OK;
 }
 
@@ -195,8 +208,8 @@ pc_status dense_jobs(pc_ctx *c, int M, int lm_mode, DenseJobs **out) {
     if (jobs.empty()) jobs.push_back(GemvJob{});
     PC_TRY(dalloc(c, jobs.size() * sizeof(GemvJob), (void **)&dj.d_jobs));
     PC_TRY(dalloc(c, counts.size() * 4, (void **)&dj.d_counts));
-    PC_CU(cudaMemcpy(dj.d_jobs, jobs.data(), jobs.size() * sizeof(GemvJob), cudaMemcpyHostToDevice));
-    PC_CU(cudaMemcpy(dj.d_counts, counts.data(), counts.size() * 4, cudaMemcpyHostToDevice));
+    PC_TRY(upload(c, dj.d_jobs, jobs.data(), jobs.size() * sizeof(GemvJob)));
+    PC_TRY(upload(c, dj.d_counts, counts.data(), counts.size() * 4));
     dj.h_jobs = jobs;
     dj.h_counts = counts;
     auto res = c->dense_jobs.emplace(key, dj);
@@ -635,7 +648,7 @@ pc_status run_step(pc_ctx *c, int M, const int *seq, int lm_mode, int nsplit_ful
             cudaMemcpy(hh.data(), c->h, hh.size() * 4, cudaMemcpyDeviceToHost);
             cudaMemcpy(aa.data(), c->tmp, aa.size() * 4, cudaMemcpyDeviceToHost);
             for (size_t i = 0; i < hh.size(); ++i) hh[i] = hh[i] + aa[i];
-            cudaMemcpy(c->h, hh.data(), hh.size() * 4, cudaMemcpyHostToDevice);
+            PC_TRY(upload(c, c->h, hh.data(), hh.size() * 4));
         }
         trace_row(c, pre + "post_attn_residual", c->h + (size_t)last * D, D);
         // the post-attention norm runs inside the router kernel, except when
@@ -1163,9 +1176,9 @@ pc_status pc_history_push(pc_ctx *c, const int *ids, int n) {
     for (int i = 0; i < n && len + (int)keep.size() < SAMPLE_HIST_CAP; ++i)
         if (ids[i] >= 0 && ids[i] < c->cfg.vocab) keep.push_back(ids[i]);
     if (keep.empty()) return PC_OK;
-    PC_CU(cudaMemcpy(c->smp.hist + len, keep.data(), keep.size() * sizeof(int), cudaMemcpyHostToDevice));
+    PC_TRY(upload(c, c->smp.hist + len, keep.data(), keep.size() * sizeof(int)));
     len += (int)keep.size();
-    PC_CU(cudaMemcpy(&c->smp.state->hist_len, &len, sizeof len, cudaMemcpyHostToDevice));
+    PC_TRY(upload(c, &c->smp.state->hist_len, &len, sizeof len));
     return PC_OK;
 }
 

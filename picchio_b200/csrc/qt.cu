@@ -56,6 +56,9 @@ pc_status jobs_for(pc_qt *w, int S, std::pair<GemvJob *, int *> &out) {
     const int n = (int)jobs.size();
     PC_CU(cudaMemcpy(dj, jobs.data(), jobs.size() * sizeof(GemvJob), cudaMemcpyHostToDevice));
     PC_CU(cudaMemcpy(dc, &n, 4, cudaMemcpyHostToDevice));
+    // a pageable copy can still be in flight on the legacy stream when
+    // cudaMemcpy returns; the caller's stream need not wait for that stream
+    PC_CU(cudaDeviceSynchronize());
     out = {dj, dc};
     w->jobs[S] = out;
     return PC_OK;
@@ -71,8 +74,10 @@ pc_status jobs_for(pc_qt *w, int S, std::pair<GemvJob *, int *> &out) {
 // every call rewrites the job count and table with a one-warp kernel before
 // the GEMV reads them, so nothing in it has to start at zero.  Nothing is
 // allocated, so two calls that overlap (different streams or threads) race on
-// it.  The GEMV has no bounded waits and reports nothing through an error
-// word; launch failures come back from the launch itself.
+// it.  The GEMV's only device-side failure is a bounded wait for a weight
+// copy giving up; it records that in an error word kept in the same scratch
+// (sticky until pc_qt_check reads and clears it).  Launch failures come back
+// from the launch itself.
 
 namespace {
 
@@ -81,6 +86,7 @@ constexpr int NOALLOC_MAX_JOBS = PC_QT_NOALLOC_MAX_ROWS / GEMV_MAXR;
 struct NoallocScratch {
     GemvJob jobs[NOALLOC_MAX_JOBS];
     int njobs;
+    int err;  // nonzero: a GEMV wait gave up (cleared by pc_qt_check)
 };
 
 __device__ __align__(256) unsigned char g_noalloc_scratch[sizeof(NoallocScratch)];
@@ -143,7 +149,8 @@ pc_status pc_qt_create(int device, int fmt, int O, int I, int block_size, const 
     if (fmt == PC_FMT_F32) {
         tile_geom(w->t, TF_F32, O, I, 0, PERM_NONE, 0);
         if ((s = qalloc(w, (size_t)O * I * 4, (void **)&w->t.f32)) != PC_OK) return done(s);
-        if (cudaMemcpy(w->t.f32, data, (size_t)O * I * 4, cudaMemcpyHostToDevice) != cudaSuccess)
+        if (cudaMemcpy(w->t.f32, data, (size_t)O * I * 4, cudaMemcpyHostToDevice) != cudaSuccess ||
+            cudaDeviceSynchronize() != cudaSuccess)
             return done(fail(PC_ERR_CUDA, "upload"));
         return done(PC_OK);
     }
@@ -254,10 +261,34 @@ pc_status pc_qt_matmul_noalloc(pc_qt *w, const float *x_dev, float *y_dev, int S
     p.ldx = w->t.I;
     p.y = y_dev;
     p.ldy = w->t.O;
-    p.err = nullptr;
+    p.err = &s->err;
     const int nt = gemv_nt_for_rows(std::min(S, GEMV_MAXR));
     if (!gemv_plan(p, nt, w->max_smem)) return fail(PC_ERR_FORMAT, "input rows do not fit in shared memory");
     PC_CU(gemv_launch(p, nt, w->nsm, st));
+    return PC_OK;
+}
+
+pc_status pc_qt_check(pc_qt *w, void *stream) {
+    if (!w) return fail(PC_ERR_INVALID_ARG, "null weight");
+    PC_CU(cudaSetDevice(w->dev));
+    PC_CU(cudaStreamSynchronize((cudaStream_t)stream));
+    int e1 = 0, e2 = 0;
+    const int zero = 0;
+    PC_CU(cudaMemcpy(&e1, w->err, 4, cudaMemcpyDeviceToHost));
+    if (e1) PC_CU(cudaMemcpy(w->err, &zero, 4, cudaMemcpyHostToDevice));  // completed below
+    NoallocScratch *sc = nullptr;
+    {
+        std::lock_guard<std::mutex> lk(g_noalloc_mu);
+        if (w->dev >= 0 && w->dev < NOALLOC_MAX_DEVICES) sc = g_noalloc_ptr[w->dev];
+    }
+    if (sc) {
+        PC_CU(cudaMemcpy(&e2, &sc->err, 4, cudaMemcpyDeviceToHost));
+        if (e2) PC_CU(cudaMemcpy(&sc->err, &zero, 4, cudaMemcpyHostToDevice));
+    }
+    if (e1 || e2) {
+        PC_CU(cudaDeviceSynchronize());  // the clearing copies have landed before any later product
+        return fail(PC_ERR_TIMEOUT, "a GEMV wait for its weight copies gave up");
+    }
     return PC_OK;
 }
 

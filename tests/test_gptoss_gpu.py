@@ -182,4 +182,7 @@ def test_moe_experts_configs1_against_oracle(model_dir, M):
     for layer in (0,):
         for r in rows:
             ref = orc.moe(x[r], layer, sel=sel[r].tolist(), wts=w[r])
+            bad = np.where(~np.isfinite(out[r]))[0]
+            assert len(bad) == 0 and np.isfinite(ref).all(), (M, r, bad[:8].tolist(), len(bad),
+                                                              bool(np.isfinite(ref).all()))
             assert rel_l2(out[r], ref) < tol, (M, r, rel_l2(out[r], ref))

@@ -38,6 +38,7 @@ def test_noalloc_equals_matmul_twice():
             ref = q.matmul(x)
             a = q.matmul_noalloc(x)
             b = q.matmul_noalloc(x)
+            q.check()  # no device-side failure recorded by either call
             torch.cuda.synchronize()
             assert torch.equal(a.view(torch.int32), ref.view(torch.int32)), (q.O, q.I, S)
             assert torch.equal(b.view(torch.int32), ref.view(torch.int32)), (q.O, q.I, S)
