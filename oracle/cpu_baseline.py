@@ -162,12 +162,14 @@ def measure_e2e(threads=None, prompt_len=64, steps=32, seed=1234) -> dict | None
         r = subprocess.run([O.REF_BIN_PATH], env=env, capture_output=True, text=True, cwd=d, timeout=300)
     if r.returncode != 0:
         return None
-    gen = re.search(r"generated (\d+) tokens in ([0-9.]+) s", r.stderr)
+    # "generated N tokens in T s (R tok/s)": R from the binary's own clock
+    # (T is printed with two decimals only)
+    gen = re.search(r"generated (\d+) tokens in ([0-9.]+) s \(([0-9.]+) tok/s\)", r.stderr)
     pre = re.search(r"prefill in ([0-9.]+) s", r.stderr)
     if not gen:
         return None
-    n, t = int(gen.group(1)), float(gen.group(2))
-    return {"value": n / t if t > 0 else None, "unit": "tok/s", "cores": threads, "kind": "reference",
+    n, rate = int(gen.group(1)), float(gen.group(3))
+    return {"value": rate if rate > 0 else None, "unit": "tok/s", "cores": threads, "kind": "reference",
             "prefill_s": float(pre.group(1)) if pre else None,
             "sample": (f"unmodified reference binary end to end on the tiny seeded model (configs[0]): "
                        f"{prompt_len}-id prompt, {n} greedy tokens, OMP_NUM_THREADS={threads}, "
