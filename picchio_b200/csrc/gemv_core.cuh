@@ -322,13 +322,13 @@ __device__ __forceinline__ void load_blk(BlkRegs &r, const uint8_t *blk, int lan
     }
 }
 
-// acc (rows g, g+8 x columns 2t, 2t+1) += group scale * exact group sum
-__device__ __forceinline__ void scale4(float (&acc)[4], const int (&d)[4], uint32_t s_g, uint32_t s_g8) {
-    const float a = __uint_as_float(s_g), b = __uint_as_float(s_g8);
-    acc[0] = __fmaf_rn(__int2float_rn(d[0]), a, acc[0]);
-    acc[1] = __fmaf_rn(__int2float_rn(d[1]), a, acc[1]);
-    acc[2] = __fmaf_rn(__int2float_rn(d[2]), b, acc[2]);
-    acc[3] = __fmaf_rn(__int2float_rn(d[3]), b, acc[3]);
+// The grouped form: acc[0] (row g), acc[2] (row g + 8) += group scale *
+// (wi * d_even + d_odd), the lane's two digit columns joined in s32 first
+// (wi = 256 where they are (hi, mid), 1 where they are (lo, zero): below
+// 2^28 in magnitude, exact), so a group costs two int-to-float conversions instead of four.
+__device__ __forceinline__ void scale2(float (&acc)[4], const int (&d)[4], uint32_t s_g, uint32_t s_g8, int wi) {
+    acc[0] = __fmaf_rn(__int2float_rn(d[0] * wi + d[1]), __uint_as_float(s_g), acc[0]);
+    acc[2] = __fmaf_rn(__int2float_rn(d[2] * wi + d[3]), __uint_as_float(s_g8), acc[2]);
 }
 
 // The same from a block staged in shared memory.
@@ -378,7 +378,7 @@ __device__ __forceinline__ void a_frags4(const uint4 &a, uint32_t (&a0)[4], uint
 
 template <int FMT, int NT, int GS>
 __device__ __forceinline__ void block_t4(const BlkRegs &r, const uint4 (&B)[NT], float (&acc)[NT][4],
-                                         int (&ia)[NT][4]) {
+                                         int (&ia)[NT][4], int wi) {
     uint32_t a0[4], a1[4];
     a_frags4<FMT>(r.a, a0, a1);
     const int M[4] = {0, 0, 0, 0};
@@ -387,22 +387,22 @@ __device__ __forceinline__ void block_t4(const BlkRegs &r, const uint4 (&B)[NT],
         int d[4];
         if (GS == 32) {
             mma_s8_16832(d, a0, B[nt].x, B[nt].y, M);
-            scale4(acc[nt], d, r.s.x, r.s.y);
+            scale2(acc[nt], d, r.s.x, r.s.y, wi);
             mma_s8_16832(d, a1, B[nt].z, B[nt].w, M);
-            scale4(acc[nt], d, r.s.z, r.s.w);
+            scale2(acc[nt], d, r.s.z, r.s.w, wi);
         } else if (GS == 64) {
             mma_s8_16832(d, a0, B[nt].x, B[nt].y, M);
             mma_s8_16832(d, a1, B[nt].z, B[nt].w, d);
-            scale4(acc[nt], d, r.s.x, r.s.y);
+            scale2(acc[nt], d, r.s.x, r.s.y, wi);
         } else if (GS == 16) {  // one group per 16 columns: the other half of B is zero
             mma_s8_16832(d, a0, B[nt].x, 0u, M);
-            scale4(acc[nt], d, r.s.x, r.s.y);
+            scale2(acc[nt], d, r.s.x, r.s.y, wi);
             mma_s8_16832(d, a0, 0u, B[nt].y, M);
-            scale4(acc[nt], d, r.s.z, r.s.w);
+            scale2(acc[nt], d, r.s.z, r.s.w, wi);
             mma_s8_16832(d, a1, B[nt].z, 0u, M);
-            scale4(acc[nt], d, r.s2.x, r.s2.y);
+            scale2(acc[nt], d, r.s2.x, r.s2.y, wi);
             mma_s8_16832(d, a1, 0u, B[nt].w, M);
-            scale4(acc[nt], d, r.s2.z, r.s2.w);
+            scale2(acc[nt], d, r.s2.z, r.s2.w, wi);
         } else {
             mma_s8_16832(ia[nt], a0, B[nt].x, B[nt].y, ia[nt]);
             mma_s8_16832(ia[nt], a1, B[nt].z, B[nt].w, ia[nt]);
@@ -785,6 +785,11 @@ __device__ __forceinline__ void gemv_cta(const GemvParams &p, uint8_t *smem, int
     float acc[NT][4];
     int ia[NT][4];
     const float W0 = (lane & 1) ? 1.0f : 65536.0f, W1 = (lane & 1) ? 0.0f : 256.0f;  // digit weights of my columns
+    // grouped 4-bit scales: the two columns are joined as WI * first + second
+    // per group (scale2), worth WJ each
+    constexpr bool JOINED = tf_4bit(FMT) && GS != 0;
+    const int WI = (lane & 1) ? 1 : 256;
+    const float WJ = (lane & 1) ? 1.0f : 256.0f;
     // one step: issue the step R - 1 ahead, wait for this one, compute it
     int seq = 0;
     auto do_step = [&](int c) {
@@ -809,7 +814,7 @@ __device__ __forceinline__ void gemv_cta(const GemvParams &p, uint8_t *smem, int
 #pragma unroll
                 for (int nt = 0; nt < NT; ++nt)
                     B[nt] = reinterpret_cast<const uint4 *>(Bsm)[(nt * p.kblocks + kc) * 32 + lane];
-                block_t4<FMT, NT, GS>(r, B, acc, ia);
+                block_t4<FMT, NT, GS>(r, B, acc, ia, WI);
             } else {
                 uint2 B[NT];
 #pragma unroll
@@ -860,8 +865,8 @@ __device__ __forceinline__ void gemv_cta(const GemvParams &p, uint8_t *smem, int
             float v[NT][2];
 #pragma unroll
             for (int nt = 0; nt < NT; ++nt) {
-                float vg = __fmaf_rn(acc[nt][1], W1, __fmul_rn(acc[nt][0], W0));
-                float vg8 = __fmaf_rn(acc[nt][3], W1, __fmul_rn(acc[nt][2], W0));
+                float vg = JOINED ? __fmul_rn(acc[nt][0], WJ) : __fmaf_rn(acc[nt][1], W1, __fmul_rn(acc[nt][0], W0));
+                float vg8 = JOINED ? __fmul_rn(acc[nt][2], WJ) : __fmaf_rn(acc[nt][3], W1, __fmul_rn(acc[nt][2], W0));
                 v[nt][0] = __fadd_rn(vg, __shfl_xor_sync(0xffffffffu, vg, 1));
                 v[nt][1] = __fadd_rn(vg8, __shfl_xor_sync(0xffffffffu, vg8, 1));
             }

@@ -397,70 +397,72 @@ __device__ __forceinline__ uint32_t sw128_off(int row, int col) {
     return (uint32_t)((row >> 3) * 1024 + (row & 7) * 128 + ((((col >> 3) ^ (row & 7)) << 4) | ((col & 7) * 2)));
 }
 
-__device__ __forceinline__ uint32_t pack_h2(float a, float b) {
-    const __half2 h = __floats2half2_rn(a, b);
-    return *reinterpret_cast<const uint32_t *>(&h);
+// f16 arithmetic on packed pairs, rounded to nearest (the explicit rounding
+// mode also keeps the two from being contracted into one fused operation).
+__device__ __forceinline__ uint32_t h2_sub(uint32_t a, uint32_t b) {
+    uint32_t d;
+    asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    return d;
 }
-
-// Two nibble values held as the floats 2^23 + n (bytes [n, 0, 0, 0x4B]) to the
-// packed f16 pair of (n - 8) * s: exact subtraction, then one fp32 multiply
-// (the reference's dequantization), both as packed f32x2 operations, then
-// round to f16.
-__device__ __forceinline__ uint32_t te_dq2(uint32_t a, uint32_t b, uint64_t s2) {
-    uint64_t v;
-    asm("mov.b64 %0, {%1, %2};" : "=l"(v) : "r"(a), "r"(b));
-    constexpr uint64_t MAGIC2 = 0x4B0000084B000008ull;  // 2^23 + 8 twice
-    v = f2_mul(f2_sub(v, MAGIC2), s2);
-    uint32_t lo, hi;
-    asm("mov.b64 {%0, %1}, %2;" : "=r"(lo), "=r"(hi) : "l"(v));
-    return pack_h2(__uint_as_float(lo), __uint_as_float(hi));
+__device__ __forceinline__ uint32_t h2_mul(uint32_t a, uint32_t b) {
+    uint32_t d;
+    asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    return d;
 }
-
-__device__ __forceinline__ uint64_t dup_f2(float s) {
-    uint64_t v;
-    asm("mov.b64 %0, {%1, %1};" : "=l"(v) : "r"(__float_as_uint(s)));
-    return v;
+__device__ __forceinline__ uint32_t h2_dup(float s) {
+    uint32_t d;
+    asm("cvt.rn.f16x2.f32 %0, %1, %1;" : "=r"(d) : "f"(s));
+    return d;
 }
 
 // Dequantizes lane L's 16 bytes of one T4 block (rows g, g + 8; columns
 // 32m + 16h + 4t + j) into the f16 tile at row tile r.  Byte j of word q holds
 // column 32m + 16h + 4t + j (q = 2m + h): row g in its low nibble, row g + 8
-// in its high nibble.
+// in its high nibble.  Each nibble n becomes the f16 1024 + n by one byte
+// permute per pair (0x64 as the high byte), then (1024 + n) - 1032 = n - 8
+// exactly, and one f16 multiply by the group scale rounded to f16: the
+// MMA's f16 operand (n - 8) * scale, within one f16 rounding of the fp32
+// product the reference forms, in under two instructions per weight.
 template <int GS>
 __device__ __forceinline__ void te_dequant_chunk(const uint8_t *blk, int L, int r, uint8_t *A) {
     const int g = L >> 2, t = L & 3;
     const uint4 w4 = *reinterpret_cast<const uint4 *>(blk + L * 16);
     const uint32_t w[4] = {w4.x, w4.y, w4.z, w4.w};
-    float sc[4][2];  // [16-column group q][row half]
+    uint32_t sc[4][2];  // [16-column group q][row half], as f16 pairs
     if (GS == 32) {
         const float4 s = *reinterpret_cast<const float4 *>(blk + 512 + g * 16);
-        sc[0][0] = sc[1][0] = s.x; sc[0][1] = sc[1][1] = s.y;
-        sc[2][0] = sc[3][0] = s.z; sc[2][1] = sc[3][1] = s.w;
+        sc[0][0] = sc[1][0] = h2_dup(s.x); sc[0][1] = sc[1][1] = h2_dup(s.y);
+        sc[2][0] = sc[3][0] = h2_dup(s.z); sc[2][1] = sc[3][1] = h2_dup(s.w);
     } else if (GS == 64) {
         const float2 s = *reinterpret_cast<const float2 *>(blk + 512 + g * 8);
+        const uint32_t a = h2_dup(s.x), b = h2_dup(s.y);
 #pragma unroll
-        for (int q = 0; q < 4; ++q) { sc[q][0] = s.x; sc[q][1] = s.y; }
+        for (int q = 0; q < 4; ++q) { sc[q][0] = a; sc[q][1] = b; }
     } else if (GS == 16) {
         const float4 s0 = *reinterpret_cast<const float4 *>(blk + 512 + g * 32);
         const float4 s1 = *reinterpret_cast<const float4 *>(blk + 512 + g * 32 + 16);
-        sc[0][0] = s0.x; sc[0][1] = s0.y; sc[1][0] = s0.z; sc[1][1] = s0.w;
-        sc[2][0] = s1.x; sc[2][1] = s1.y; sc[3][0] = s1.z; sc[3][1] = s1.w;
+        sc[0][0] = h2_dup(s0.x); sc[0][1] = h2_dup(s0.y); sc[1][0] = h2_dup(s0.z); sc[1][1] = h2_dup(s0.w);
+        sc[2][0] = h2_dup(s1.x); sc[2][1] = h2_dup(s1.y); sc[3][0] = h2_dup(s1.z); sc[3][1] = h2_dup(s1.w);
     } else {  // per-row scale: applied in the epilogue
 #pragma unroll
-        for (int q = 0; q < 4; ++q) { sc[q][0] = 1.0f; sc[q][1] = 1.0f; }
+        for (int q = 0; q < 4; ++q) { sc[q][0] = 0x3C003C00u; sc[q][1] = 0x3C003C00u; }  // 1.0
     }
+    constexpr uint32_t C1032 = 0x64086408u;  // the f16 pair (1032, 1032)
 #pragma unroll
     for (int q = 0; q < 4; ++q) {  // word q = 2m + h
         const int col = 32 * (q >> 1) + 16 * (q & 1) + 4 * t;
 #pragma unroll
         for (int rh = 0; rh < 2; ++rh) {
             const uint32_t nib = (w[q] >> (4 * rh)) & 0x0F0F0F0Fu;  // byte j = n of column j
-            // byte j of nib into byte 0, zeros, 0x4B into byte 3: the float 2^23 + n
-            const uint32_t f0 = __byte_perm(nib, 0x4B000000u, 0x7540), f1 = __byte_perm(nib, 0x4B000000u, 0x7541);
-            const uint32_t f2 = __byte_perm(nib, 0x4B000000u, 0x7542), f3 = __byte_perm(nib, 0x4B000000u, 0x7543);
-            const uint64_t s2 = dup_f2(sc[q][rh]);
+            // columns (0, 1) and (2, 3) as the f16 pairs 1024 + n
+            const uint32_t v01 = __byte_perm(nib, 0x64646464u, 0x4140), v23 = __byte_perm(nib, 0x64646464u, 0x4342);
+            uint32_t h01 = h2_sub(v01, C1032), h23 = h2_sub(v23, C1032);
+            if (GS != 0) {
+                h01 = h2_mul(h01, sc[q][rh]);
+                h23 = h2_mul(h23, sc[q][rh]);
+            }
             const int row = r * 16 + g + 8 * rh;
-            *reinterpret_cast<uint2 *>(A + sw128_off(row, col)) = make_uint2(te_dq2(f0, f1, s2), te_dq2(f2, f3, s2));
+            *reinterpret_cast<uint2 *>(A + sw128_off(row, col)) = make_uint2(h01, h23);
         }
     }
 }
