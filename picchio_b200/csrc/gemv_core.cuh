@@ -803,9 +803,7 @@ __device__ __forceinline__ void gemv_cta(const GemvParams &p, uint8_t *smem, int
         for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
             for (int i = 0; i < 4; ++i) ia[nt][i] = 0;
-#pragma unroll
-        for (int i = 0; i < MB; ++i) {
-            if (i >= nb) break;
+        auto block = [&](int i) {
             const int kc = kb0 + c * MB + i;
             BlkRegs r;
             load_blk_smem<FMT, GS>(r, slot + i * BB, lane);
@@ -821,6 +819,16 @@ __device__ __forceinline__ void gemv_cta(const GemvParams &p, uint8_t *smem, int
                 for (int nt = 0; nt < NT; ++nt) B[nt] = Bsm[(nt * p.kblocks + kc) * 32 + lane];
                 block_t8<NT>(r, B, ia);
             }
+        };
+        // A full step runs its blocks with no per-block bound check (the
+        // check and its branch cost more than 1 % of the decode step); only
+        // the last step of a warp's share of a unit can be partial.
+        if (nb == MB) {
+#pragma unroll
+            for (int i = 0; i < MB; ++i) block(i);
+        } else {
+#pragma unroll 1
+            for (int i = 0; i < nb; ++i) block(i);
         }
         __syncwarp();  // every lane is done with the slot before it is refilled
         if (FMT == TF_T8 || GS == 0) {  // per-row scale: the step's exact sums join the fp32 accumulator
