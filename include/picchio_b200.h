@@ -263,7 +263,10 @@ pc_status pc_expert_stats(pc_ctx *ctx, uint64_t *hits, uint64_t *misses, uint64_
  * (the decoded E8M0 factors, 2^(e - 127)). */
 pc_status pc_qt_create(int device, int fmt, int O, int I, int block_size, const void *data,
                        const float *scales, pc_qt **out);
-/* y_dev[S][O] = x_dev[S][I] . W^T on `stream` (a cudaStream_t, NULL = default). */
+/* y_dev[S][O] = x_dev[S][I] . W^T on `stream` (a cudaStream_t, NULL = default).
+ * Up to 8 rows share one pass over the weights; when their padded input rows
+ * do not fit one CTA's shared memory together (INT4 beyond ~4100 columns at
+ * 3-8 rows), the rows run as jobs of two, each job streaming the weights. */
 pc_status pc_qt_matmul(pc_qt *w, const float *x_dev, float *y_dev, int S, void *stream);
 /* The same product as pc_qt_matmul, bit for bit, for callers that must not
  * allocate device memory during the call: code running under a memory budget
@@ -276,7 +279,9 @@ pc_status pc_qt_matmul(pc_qt *w, const float *x_dev, float *y_dev, int S, void *
  * address (cudaGetSymbolAddress) - make that first call before any stream
  * capture that would include it.  Every call rewrites the whole table before
  * the GEMV reads it.
- * Limits: S <= PC_QT_NOALLOC_MAX_ROWS (PC_ERR_RANGE beyond); one scratch per
+ * Limits: S <= PC_QT_NOALLOC_MAX_ROWS (PC_ERR_RANGE beyond); rows that
+ * pc_qt_matmul would split into two-row jobs (see above) are refused with
+ * PC_ERR_FORMAT; one scratch per
  * device, so calls that overlap in time (other streams or threads) race and
  * must be serialized by the caller.  This entry point has no counterpart in
  * the reference. */

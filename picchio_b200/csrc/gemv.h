@@ -9,12 +9,15 @@ namespace pc {
 constexpr int GEMV_CONSUMERS = 12;
 // k-blocks per step of a warp (64-column T4 or 32-column T8 blocks), and the
 // depth of its shared-memory ring of steps; both shrink with the N-tiles so
-// that the B operand and the rings fit in one CTA's shared memory.
-__host__ __device__ constexpr int gemv_step_blocks(int fmt, int nt) { return nt == 4 ? 2 : (tf_4bit(fmt) ? 4 : 8); }
-// (T4 with two N-tiles: 3 steps, which bounds its padded input length at 6368.)
-__host__ __device__ constexpr int gemv_ring_depth(int fmt, int nt) {
-    return nt == 1 ? (tf_4bit(fmt) ? 4 : 3) : (nt == 2 && tf_4bit(fmt)) ? 3 : 2;
+// that the B operand and the rings fit in one CTA's shared memory.  4-bit
+// blocks with two N-tiles (batched decode jobs) take 8-block steps in a
+// 2-deep ring: the same bytes in flight as 4-block steps 3 deep, half the
+// per-step work (bs64 decode +13 %); a padded input row of up to ~4100
+// columns fits (gs32), longer ones run as one-N-tile jobs (pc_qt_matmul).
+__host__ __device__ constexpr int gemv_step_blocks(int fmt, int nt) {
+    return nt == 4 ? 2 : (tf_4bit(fmt) ? (nt == 2 ? 8 : 4) : 8);
 }
+__host__ __device__ constexpr int gemv_ring_depth(int fmt, int nt) { return nt == 1 ? (tf_4bit(fmt) ? 4 : 3) : 2; }
 // N-tiles (8 MMA columns = 2 input rows x 4 digit columns) for a job of `rows` input rows
 inline int gemv_nt_for_rows(int rows) { return rows <= 2 ? 1 : rows <= 4 ? 2 : 4; }
 constexpr int GEMV_THREADS = 32 * GEMV_CONSUMERS;

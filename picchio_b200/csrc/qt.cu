@@ -34,18 +34,20 @@ pc_status qalloc(pc_qt *w, size_t bytes, void **out) {
     return cudaMemset(*out, 0, bytes ? bytes : 16) == cudaSuccess ? PC_OK : fail(PC_ERR_CUDA, "cudaMemset");
 }
 
-pc_status jobs_for(pc_qt *w, int S, std::pair<GemvJob *, int *> &out) {
-    auto it = w->jobs.find(S);
+// Device job table for S input rows, `per` rows per job (cached per pair).
+pc_status jobs_for(pc_qt *w, int S, int per, std::pair<GemvJob *, int *> &out) {
+    const int key = S * 16 + per;
+    auto it = w->jobs.find(key);
     if (it != w->jobs.end()) { out = it->second; return PC_OK; }
     std::vector<GemvJob> jobs;
-    for (int r0 = 0; r0 < S; r0 += GEMV_MAXR) {
+    for (int r0 = 0; r0 < S; r0 += per) {
         GemvJob j;
         memset(&j, 0, sizeof j);
         j.tiles = w->t.tiles;
         j.rs = w->t.rs;
         j.n_rt = w->t.Op / 16;
         j.O = w->t.O;
-        j.nrows = std::min(GEMV_MAXR, S - r0);
+        j.nrows = std::min(per, S - r0);
         for (int i = 0; i < j.nrows; ++i) j.in_row[i] = j.out_row[i] = r0 + i;
         jobs.push_back(j);
     }
@@ -60,7 +62,7 @@ pc_status jobs_for(pc_qt *w, int S, std::pair<GemvJob *, int *> &out) {
     // cudaMemcpy returns; the caller's stream need not wait for that stream
     PC_CU(cudaDeviceSynchronize());
     out = {dj, dc};
-    w->jobs[S] = out;
+    w->jobs[key] = out;
     return PC_OK;
 }
 
@@ -189,8 +191,18 @@ pc_status pc_qt_matmul(pc_qt *w, const float *x_dev, float *y_dev, int S, void *
         PC_CU(launch_gemv_f32(f, st));
         return PC_OK;
     }
+    // The B operand of all rows (up to 8, four N-tiles) and the weight rings
+    // must fit in one CTA's shared memory; a long input row that does not fit
+    // with the N-tiles its row count needs runs as jobs of two rows on one
+    // N-tile (the weights are then streamed once per job).
+    int nt = gemv_nt_for_rows(std::min(S, GEMV_MAXR));
+    int per = GEMV_MAXR;
+    if (nt > 1 && gemv_smem_bytes(w->t.fmt, nt, w->t.Ip, w->t.blk_bytes) > (size_t)w->max_smem) {
+        nt = 1;
+        per = 2;
+    }
     std::pair<GemvJob *, int *> j;
-    PC_TRY(jobs_for(w, S, j));
+    PC_TRY(jobs_for(w, S, per, j));
     GemvParams p{};
     p.jobs = j.first;
     p.njobs = j.second;
@@ -203,7 +215,7 @@ pc_status pc_qt_matmul(pc_qt *w, const float *x_dev, float *y_dev, int S, void *
     p.perm = PERM_NONE;
     p.epi = EPI_STORE;
     p.static_jobs = 1;
-    if (S <= GEMV_MAXR) {  // one job, carried in the launch; all rows in the B operand
+    if (S <= per) {  // one job, carried in the launch; all rows in the B operand
         GemvJob jb;
         memset(&jb, 0, sizeof jb);
         jb.tiles = w->t.tiles;
@@ -221,7 +233,6 @@ pc_status pc_qt_matmul(pc_qt *w, const float *x_dev, float *y_dev, int S, void *
     p.y = y_dev;
     p.ldy = w->t.O;
     p.err = w->err;
-    const int nt = gemv_nt_for_rows(std::min(S, GEMV_MAXR));
     if (!gemv_plan(p, nt, w->max_smem)) return fail(PC_ERR_FORMAT, "input rows do not fit in shared memory");
     PC_CU(gemv_launch(p, nt, w->nsm, st));
     return PC_OK;

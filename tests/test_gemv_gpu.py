@@ -30,8 +30,10 @@ def bits(a):
     return np.ascontiguousarray(a, np.float32).view(np.uint32)
 
 
+# (40, 6000, 32): from 3 input rows the B operand of a long row and the weight
+# rings no longer fit one CTA's shared memory; the product runs as jobs of two rows.
 SHAPES = [(64, 256, 32), (48, 2880, 32), (5760, 2880, 32), (2880, 2880, 64), (40, 320, 64),
-          (33, 100, 32), (17, 96, 16), (16, 768, 0), (29, 131, 0)]
+          (33, 100, 32), (17, 96, 16), (16, 768, 0), (29, 131, 0), (40, 6000, 32)]
 
 
 @pytest.mark.parametrize("shape", SHAPES)
