@@ -86,6 +86,18 @@ __device__ __forceinline__ void gemv_bulk_load(void *dst, const void *src, uint3
                  "l"(src), "r"(bytes), "r"(smem_u32(bar))
                  : "memory");
 }
+// A step copied by the lanes with cp.async (tiles that may sit in mapped
+// host memory, streamed residency), arriving on bar.  Out of line: kept off
+// the resident path's code, which is bound by instruction fetch in short
+// launches (bs64 decode +1.2 %, bs1 +0.4 %).
+__device__ __noinline__ void gemv_lanes_copy(uint8_t *dst, const uint8_t *src, int nb, int BB, int sbytes, int lane,
+                                             uint64_t *bar) {
+    for (int i = 0; i < nb; ++i) {
+        cp_async16(dst + i * BB + lane * 16, src + (size_t)i * BB + lane * 16);
+        if (lane * 16 < sbytes) cp_async16(dst + i * BB + 512 + lane * 16, src + (size_t)i * BB + 512 + lane * 16);
+    }
+    cp_async_mbar_arrive(bar);
+}
 // Bounded wait for phase `parity` of bar; false when the bound ran out.
 __device__ __forceinline__ bool gemv_mbar_wait(uint64_t *bar, uint32_t parity) {
     if (mbar_try_wait(bar, parity)) return true;
@@ -733,15 +745,7 @@ __device__ __forceinline__ void gemv_cta(const GemvParams &p, uint8_t *smem, int
             uint8_t *dst = myring + (size_t)(ld_seq % R) * MB * BB;
             const uint8_t *src = slice(ld_u, ld_j) + (size_t)ld_c * MB * BB;
             if (lanes_copy) {
-#pragma unroll
-                for (int i = 0; i < MB; ++i) {
-                    if (i < nb) {
-                        cp_async16(dst + i * BB + lane * 16, src + (size_t)i * BB + lane * 16);
-                        if (lane * 16 < sbytes)
-                            cp_async16(dst + i * BB + 512 + lane * 16, src + (size_t)i * BB + 512 + lane * 16);
-                    }
-                }
-                cp_async_mbar_arrive(bar);
+                gemv_lanes_copy(dst, src, nb, BB, sbytes, lane, bar);
             } else if (lane == 0) {
                 if (nb > 0) {
                     mbar_arrive_expect_tx(bar, (uint32_t)(nb * BB));
